@@ -1,0 +1,523 @@
+// sd_api.cu -- the C ABI (include/sparse_decode.h): index lifetime, cache
+// writes, decode launches and the sharded decode steps. Host code only; the
+// kernels live in sd_decode.cuh / sd_update.cuh, instantiated by sd_inst.cu.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/sparse_decode.h"
+#include "sd_format.h"
+#include "sd_kernels.h"
+#include "sd_params.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t fail(int32_t status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+#define SD_CUDA(call)                                                                              \
+  do {                                                                                             \
+    cudaError_t e_ = (call);                                                                       \
+    if (e_ != cudaSuccess) return fail(SD_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                       __FILE__, __LINE__);                                        \
+  } while (0)
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int elt_size(int dtype) { return dtype == SD_F32 ? 4 : 2; }
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+sd::KernelSet lookup(int dtype, int bits, int D, int G) {
+  const int key = dtype * 16 + bits;
+  switch (key) {
+    case 0 * 16 + 0: return sd::kernels_e0_b0(D, G);
+    case 1 * 16 + 0: return sd::kernels_e1_b0(D, G);
+    case 2 * 16 + 0: return sd::kernels_e2_b0(D, G);
+    case 0 * 16 + 4: return sd::kernels_e0_b4(D, G);
+    case 1 * 16 + 4: return sd::kernels_e1_b4(D, G);
+    case 2 * 16 + 4: return sd::kernels_e2_b4(D, G);
+    case 0 * 16 + 8: return sd::kernels_e0_b8(D, G);
+    case 1 * 16 + 8: return sd::kernels_e1_b8(D, G);
+    case 2 * 16 + 8: return sd::kernels_e2_b8(D, G);
+    default: return sd::KernelSet{nullptr, nullptr, nullptr, nullptr};
+  }
+}
+
+}  // namespace
+
+struct sd_index {
+  sd_config cfg;
+  int device;
+  int G, groups, esize, row_bytes;
+  int64_t cap_global, nb_global;
+  int64_t cap_local, nb_local;
+  int64_t offset;
+  int C;
+  size_t smem;
+  void* arena;
+  size_t arena_bytes;
+  void *k_data, *v_data, *k_scales, *k_biases, *v_scales, *v_biases, *summ;
+  int* d_err;
+  CUtensorMap tmK, tmV;
+  sd::KernelSet ks;
+  bool attrs_set;
+};
+
+namespace {
+
+int32_t validate(const sd_config* c) {
+  if (!c) return fail(SD_ERR_INVALID_ARG, "config is NULL");
+  if (c->batch < 1 || c->n_q_heads < 1 || c->n_kv_heads < 1 || c->capacity < 1)
+    return fail(SD_ERR_INVALID_ARG, "batch, n_q_heads, n_kv_heads and capacity must be positive");
+  if (c->n_q_heads % c->n_kv_heads != 0)
+    return fail(SD_ERR_SHAPE, "n_q_heads (%d) is not a multiple of n_kv_heads (%d)", c->n_q_heads, c->n_kv_heads);
+  const int G = c->n_q_heads / c->n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return fail(SD_ERR_SHAPE, "query heads per kv head must be 1, 2, 4 or 8 (got %d)", G);
+  if (c->head_dim != 64 && c->head_dim != 128) return fail(SD_ERR_SHAPE, "head_dim must be 64 or 128 (got %d)", c->head_dim);
+  if (c->block_size != 32 && c->block_size != 64 && c->block_size != 128 && c->block_size != 256)
+    return fail(SD_ERR_SHAPE, "block_size must be 32, 64, 128 or 256 (got %d)", c->block_size);
+  if (c->top_k < 0 || c->top_k > sd::kMaxTopK) return fail(SD_ERR_SHAPE, "top_k must be in [0, %d] (got %d)", sd::kMaxTopK, c->top_k);
+  if (c->dtype != SD_F32 && c->dtype != SD_F16 && c->dtype != SD_BF16) return fail(SD_ERR_INVALID_ARG, "unknown dtype %d", c->dtype);
+  if (c->kv_bits != 0 && c->kv_bits != 4 && c->kv_bits != 8) return fail(SD_ERR_SHAPE, "kv_bits must be 0, 4 or 8 (got %d)", c->kv_bits);
+  if (c->kv_bits != 0 && c->group_size != 64) return fail(SD_ERR_SHAPE, "group_size must be 64 for quantized caches (got %d)", c->group_size);
+  if (c->shard_count < 1 || c->shard_count > 64) return fail(SD_ERR_INVALID_ARG, "shard_count must be in [1, 64]");
+  if (c->shard_rank < 0 || c->shard_rank >= c->shard_count) return fail(SD_ERR_INVALID_ARG, "shard_rank out of range");
+  if (c->cluster_size < 0 || c->cluster_size > 16 || (c->cluster_size & (c->cluster_size - 1)) != 0)
+    return fail(SD_ERR_INVALID_ARG, "cluster_size must be 0 or a power of two <= 16");
+  for (int r : c->reserved)
+    if (r != 0) return fail(SD_ERR_INVALID_ARG, "reserved config fields must be 0");
+  if (c->shard_count * c->top_k > sd::kUnionMax)
+    return fail(SD_ERR_SHAPE, "shard_count * top_k must be <= %d", sd::kUnionMax);
+  return SD_OK;
+}
+
+int32_t encode_map(CUtensorMap* map, void* base, int row_bytes, int64_t rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(SD_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const int box_bytes = std::min(row_bytes, 128);
+  CUtensorMapSwizzle sw = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : CU_TENSOR_MAP_SWIZZLE_32B;
+  cuuint64_t dims[2] = {cuuint64_t(row_bytes), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
+  cuuint32_t box[2] = {cuuint32_t(box_bytes), cuuint32_t(sd::kTileTokens)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return SD_OK;
+}
+
+// Number of clusters of size C the device can hold at once (0 = not launchable).
+int max_active_clusters(const sd_index* x, int C) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(C), unsigned(x->cfg.batch * x->cfg.n_kv_heads), 1);
+  cfg.blockDim = dim3(sd::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = x->smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, x->ks.decode, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int32_t setup_kernels(sd_index* x) {
+  if (x->attrs_set) return SD_OK;
+  SD_CUDA(cudaFuncSetAttribute(x->ks.decode, cudaFuncAttributeMaxDynamicSharedMemorySize, int(x->smem)));
+  SD_CUDA(cudaFuncSetAttribute(x->ks.decode, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  // An automatically chosen cluster that the device cannot co-schedule is
+  // halved; an explicitly requested one is an error.
+  while (max_active_clusters(x, x->C) < 1) {
+    if (x->cfg.cluster_size != 0 || x->C == 1)
+      return fail(SD_ERR_SHAPE, "cluster size %d cannot be scheduled with %zu bytes of shared memory", x->C, x->smem);
+    x->C /= 2;
+  }
+  x->attrs_set = true;
+  return SD_OK;
+}
+
+// Choose the cluster size: enough CTAs to cover the SMs once, capped by the
+// union buffer, and at least enough that one CTA scores <= kLocalKeysMax blocks.
+int choose_cluster(const sd_config& c, int64_t nb_local, int n_sm) {
+  const int64_t BH = int64_t(c.batch) * c.n_kv_heads;
+  int C = c.cluster_size;
+  if (C == 0) {
+    C = 1;
+    while (C < 16 && BH * C * 2 <= n_sm) C *= 2;
+  }
+  while (C > 1 && int64_t(C) * c.top_k > sd::kUnionMax) C /= 2;
+  while (C < 16 && (nb_local + C - 1) / C > sd::kLocalKeysMax) C *= 2;
+  return C;
+}
+
+int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k_new, const void* v_new,
+                      float scale, void* out, int32_t* sel_out, float* scores_out, float* cand_score,
+                      int32_t* cand_block, float* part_ml, float* part_o, cudaStream_t st) {
+  int32_t rc = setup_kernels(x);
+  if (rc != SD_OK) return rc;
+  const sd_config& c = x->cfg;
+  sd::DecodeParams p{};
+  p.B = c.batch; p.Hq = c.n_q_heads; p.Hkv = c.n_kv_heads; p.S = c.block_size; p.K = c.top_k;
+  p.T = T;
+  p.NB = (T + c.block_size - 1) / c.block_size;
+  p.P = c.shard_count; p.pr = c.shard_rank;
+  p.cap_local = int(x->cap_local);
+  p.nb_stride = int(x->nb_local);
+  p.C = x->C;
+  p.mode = mode;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.q = q; p.k_new = k_new; p.v_new = v_new;
+  p.k_data = x->k_data; p.v_data = x->v_data;
+  p.k_scales = x->k_scales; p.k_biases = x->k_biases; p.v_scales = x->v_scales; p.v_biases = x->v_biases;
+  p.summ = x->summ;
+  p.out = out; p.sel_out = sel_out; p.scores_out = scores_out;
+  p.cand_score = cand_score; p.cand_block = cand_block; p.part_ml = part_ml; p.part_o = part_o;
+  p.err = x->d_err;
+  const int64_t ncand = p.NB - 1;
+  const int64_t nloc = ncand > p.pr ? (ncand - p.pr + p.P - 1) / p.P : 0;
+  if ((nloc + x->C - 1) / x->C > sd::kLocalKeysMax)
+    return fail(SD_ERR_SHAPE, "too many blocks per CTA (%lld) for cluster size %d", (long long)((nloc + x->C - 1) / x->C), x->C);
+
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(x->C), unsigned(c.batch * c.n_kv_heads), 1);
+  cfg.blockDim = dim3(sd::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = x->smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(x->C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[3] = {&p, &x->tmK, &x->tmV};
+  SD_CUDA(cudaLaunchKernelExC(&cfg, x->ks.decode, args));
+  return SD_OK;
+}
+
+int32_t launch_summaries(sd_index* x, int64_t jl0, int64_t jl1, int64_t T, cudaStream_t st) {
+  if (jl1 <= jl0) return SD_OK;
+  const sd_config& c = x->cfg;
+  sd::SummaryParams sp{};
+  sp.Hkv = c.n_kv_heads; sp.S = c.block_size; sp.P = c.shard_count; sp.pr = c.shard_rank;
+  sp.cap_local = int(x->cap_local); sp.nb_stride = int(x->nb_local);
+  sp.T = int(T);
+  sp.jl0 = int(jl0);
+  sp.k_data = x->k_data; sp.k_scales = x->k_scales; sp.k_biases = x->k_biases; sp.summ = x->summ;
+  void* args[1] = {&sp};
+  SD_CUDA(cudaLaunchKernel(x->ks.summary, dim3(unsigned(jl1 - jl0), unsigned(c.batch * c.n_kv_heads)), dim3(128),
+                           args, 0, st));
+  return SD_OK;
+}
+
+// Local blocks [jl0, jl1) of this shard whose global index falls in [jg0, jg1].
+void local_range(const sd_index* x, int64_t jg0, int64_t jg1, int64_t* jl0, int64_t* jl1) {
+  const int64_t P = x->cfg.shard_count, pr = x->cfg.shard_rank;
+  int64_t a = jg0 <= pr ? 0 : (jg0 - pr + P - 1) / P;
+  int64_t b = jg1 < pr ? -1 : (jg1 - pr) / P;
+  *jl0 = a;
+  *jl1 = std::max(a, b + 1);
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t sd_abi_version(void) { return 1; }
+
+const char* sd_status_string(int32_t s) {
+  switch (s) {
+    case SD_OK: return "SD_OK";
+    case SD_ERR_INVALID_ARG: return "SD_ERR_INVALID_ARG";
+    case SD_ERR_SHAPE: return "SD_ERR_SHAPE";
+    case SD_ERR_CAPACITY: return "SD_ERR_CAPACITY";
+    case SD_ERR_STATE: return "SD_ERR_STATE";
+    case SD_ERR_CUDA: return "SD_ERR_CUDA";
+    case SD_ERR_DEVICE: return "SD_ERR_DEVICE";
+    default: return "SD_ERR_UNKNOWN";
+  }
+}
+
+const char* sd_last_error(void) { return g_last_error.c_str(); }
+
+int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
+  if (!out) return fail(SD_ERR_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  int32_t rc = validate(cfg);
+  if (rc != SD_OK) return rc;
+  const sd_config& c = *cfg;
+  sd_index* x = new sd_index();
+  x->cfg = c;
+  SD_CUDA(cudaGetDevice(&x->device));
+  x->G = c.n_q_heads / c.n_kv_heads;
+  x->esize = elt_size(c.dtype);
+  x->groups = c.kv_bits ? c.head_dim / 64 : 1;
+  x->row_bytes = c.kv_bits ? c.head_dim * c.kv_bits / 8 : c.head_dim * x->esize;
+  x->cap_global = (int64_t(c.capacity) + 255) / 256 * 256;
+  x->nb_global = x->cap_global / c.block_size;
+  x->nb_local = (x->nb_global + c.shard_count - 1) / c.shard_count;
+  x->cap_local = x->nb_local * c.block_size;
+  x->offset = 0;
+  const int64_t BH = int64_t(c.batch) * c.n_kv_heads;
+  if (BH * x->cap_local >= (int64_t(1) << 31) || BH > 65535) {
+    delete x;
+    return fail(SD_ERR_SHAPE, "cache too large: batch*kv_heads*capacity rows must stay below 2^31");
+  }
+  x->ks = lookup(c.dtype, c.kv_bits, c.head_dim, x->G);
+  if (!x->ks.decode) {
+    delete x;
+    return fail(SD_ERR_SHAPE, "no kernel for dtype %d, bits %d, head_dim %d, G %d", c.dtype, c.kv_bits, c.head_dim, x->G);
+  }
+  int n_sm = 148;
+  cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, x->device);
+  x->C = choose_cluster(c, x->nb_local, n_sm);
+  const sd::Layout L = sd::make_layout(c.head_dim, x->G, x->groups);
+  x->smem = size_t(L.total) + 1024;
+
+  const size_t kv = align256(size_t(BH) * x->cap_local * x->row_bytes);
+  const size_t sb = c.kv_bits ? align256(size_t(BH) * x->cap_local * x->groups * x->esize) : 0;
+  const size_t su = align256(size_t(BH) * x->nb_local * c.head_dim * x->esize);
+  x->arena_bytes = 2 * kv + 4 * sb + su + 256;
+  cudaError_t e = cudaMalloc(&x->arena, x->arena_bytes);
+  if (e != cudaSuccess) {
+    delete x;
+    return fail(SD_ERR_CUDA, "cudaMalloc(%zu) failed: %s", x->arena_bytes, cudaGetErrorString(e));
+  }
+  uint8_t* a = static_cast<uint8_t*>(x->arena);
+  x->k_data = a; a += kv;
+  x->v_data = a; a += kv;
+  if (c.kv_bits) {
+    x->k_scales = a; a += sb;
+    x->k_biases = a; a += sb;
+    x->v_scales = a; a += sb;
+    x->v_biases = a; a += sb;
+  }
+  x->summ = a; a += su;
+  x->d_err = reinterpret_cast<int*>(a);
+  e = cudaMemset(x->arena, 0, x->arena_bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(x->arena);
+    delete x;
+    return fail(SD_ERR_CUDA, "cudaMemset failed: %s", cudaGetErrorString(e));
+  }
+  rc = encode_map(&x->tmK, x->k_data, x->row_bytes, BH * x->cap_local);
+  if (rc == SD_OK) rc = encode_map(&x->tmV, x->v_data, x->row_bytes, BH * x->cap_local);
+  if (rc != SD_OK) {
+    cudaFree(x->arena);
+    delete x;
+    return rc;
+  }
+  *out = x;
+  return SD_OK;
+}
+
+int32_t sd_index_destroy(sd_index* x) {
+  if (!x) return SD_OK;
+  cudaError_t e = cudaFree(x->arena);
+  delete x;
+  if (e != cudaSuccess) return fail(SD_ERR_CUDA, "cudaFree failed: %s", cudaGetErrorString(e));
+  return SD_OK;
+}
+
+int32_t sd_index_config(const sd_index* x, sd_config* out) {
+  if (!x || !out) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  *out = x->cfg;
+  out->cluster_size = x->C;
+  return SD_OK;
+}
+
+int32_t sd_index_arrays(const sd_index* x, sd_arrays* out) {
+  if (!x || !out) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  std::memset(out, 0, sizeof(*out));
+  out->k_data = x->k_data; out->v_data = x->v_data;
+  out->k_scales = x->k_scales; out->k_biases = x->k_biases; out->v_scales = x->v_scales; out->v_biases = x->v_biases;
+  out->summaries = x->summ;
+  out->cap_local = x->cap_local;
+  out->nb_local = x->nb_local;
+  out->row_bytes = x->row_bytes;
+  out->cluster_size = x->C;
+  out->smem_bytes = int32_t(x->smem);
+  return SD_OK;
+}
+
+int32_t sd_index_offset(const sd_index* x, int64_t* offset) {
+  if (!x || !offset) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  *offset = x->offset;
+  return SD_OK;
+}
+
+int32_t sd_index_copy(const sd_index* src, sd_index** out, sd_stream stream) {
+  if (!src || !out) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  int32_t rc = sd_index_create(&src->cfg, out);
+  if (rc != SD_OK) return rc;
+  sd_index* x = *out;
+  SD_CUDA(cudaMemcpyAsync(x->arena, src->arena, src->arena_bytes - 256, cudaMemcpyDeviceToDevice,
+                          static_cast<cudaStream_t>(stream)));
+  x->offset = src->offset;
+  return SD_OK;
+}
+
+int32_t sd_append(sd_index* x, const void* keys, const void* values, int32_t n, sd_stream stream) {
+  if (!x || !keys || !values) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  if (n < 0) return fail(SD_ERR_INVALID_ARG, "n_tokens must be >= 0");
+  if (n == 0) return SD_OK;
+  if (x->offset + n > x->cap_global)
+    return fail(SD_ERR_CAPACITY, "append of %d tokens at offset %lld exceeds capacity %lld", n,
+                (long long)x->offset, (long long)x->cap_global);
+  const sd_config& c = x->cfg;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  sd::AppendParams ap{};
+  ap.Hkv = c.n_kv_heads; ap.S = c.block_size; ap.P = c.shard_count; ap.pr = c.shard_rank;
+  ap.cap_local = int(x->cap_local);
+  ap.n_tok = n;
+  ap.t0 = int(x->offset);
+  ap.k_src = keys; ap.v_src = values;
+  ap.k_data = x->k_data; ap.v_data = x->v_data;
+  ap.k_scales = x->k_scales; ap.k_biases = x->k_biases; ap.v_scales = x->v_scales; ap.v_biases = x->v_biases;
+  void* args[1] = {&ap};
+  SD_CUDA(cudaLaunchKernel(x->ks.append, dim3(unsigned((n + 3) / 4), unsigned(c.batch * c.n_kv_heads)), dim3(256),
+                           args, 0, st));
+  const int64_t T = x->offset + n;
+  int64_t jl0, jl1;
+  local_range(x, x->offset / c.block_size, (T - 1) / c.block_size, &jl0, &jl1);
+  int32_t rc = launch_summaries(x, jl0, jl1, T, st);
+  if (rc != SD_OK) return rc;
+  x->offset = T;
+  return SD_OK;
+}
+
+int32_t sd_trim(sd_index* x, int32_t n, int32_t* trimmed) {
+  if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
+  if (n < 0) return fail(SD_ERR_INVALID_ARG, "n must be >= 0");
+  const int64_t t = std::min<int64_t>(x->offset, n);
+  x->offset -= t;
+  if (trimmed) *trimmed = int32_t(t);
+  return SD_OK;
+}
+
+int32_t sd_set_offset(sd_index* x, int64_t offset) {
+  if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
+  if (offset < 0 || offset > x->cap_global) return fail(SD_ERR_CAPACITY, "offset %lld out of range", (long long)offset);
+  x->offset = offset;
+  return SD_OK;
+}
+
+int32_t sd_rebuild_summaries(sd_index* x, sd_stream stream) {
+  if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
+  if (x->offset == 0) return SD_OK;
+  int64_t jl0, jl1;
+  local_range(x, 0, (x->offset - 1) / x->cfg.block_size, &jl0, &jl1);
+  return launch_summaries(x, jl0, jl1, x->offset, static_cast<cudaStream_t>(stream));
+}
+
+int32_t sd_decode(sd_index* x, const void* q, const void* k_new, const void* v_new, float scale, void* out,
+                  int32_t* sel_out, float* scores_out, sd_stream stream) {
+  if (!x || !q || !out) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  if ((k_new == nullptr) != (v_new == nullptr)) return fail(SD_ERR_INVALID_ARG, "k_new and v_new must both be given or both NULL");
+  if (x->cfg.shard_count != 1) return fail(SD_ERR_STATE, "sd_decode needs a single-shard index; use sd_shard_*");
+  if (!std::isfinite(scale)) return fail(SD_ERR_INVALID_ARG, "scale must be finite");
+  const int64_t T = x->offset + (k_new ? 1 : 0);
+  if (T > x->cap_global) return fail(SD_ERR_CAPACITY, "decode append exceeds capacity %lld", (long long)x->cap_global);
+  if (T < 1) return fail(SD_ERR_STATE, "decode on an empty cache");
+  int32_t rc = launch_decode(x, sd::MODE_FUSED, int(T), q, k_new, v_new, scale, out, sel_out, scores_out, nullptr,
+                             nullptr, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+  if (rc == SD_OK) x->offset = T;
+  return rc;
+}
+
+int32_t sd_shard_candidates(sd_index* x, const void* q, const void* k_new, const void* v_new, float scale,
+                            float* cand_score, int32_t* cand_block, float* scores_out, sd_stream stream) {
+  if (!x || !q || !cand_score || !cand_block) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  if ((k_new == nullptr) != (v_new == nullptr)) return fail(SD_ERR_INVALID_ARG, "k_new and v_new must both be given or both NULL");
+  if (!std::isfinite(scale)) return fail(SD_ERR_INVALID_ARG, "scale must be finite");
+  const int64_t T = x->offset + (k_new ? 1 : 0);
+  if (T > x->cap_global) return fail(SD_ERR_CAPACITY, "decode append exceeds capacity %lld", (long long)x->cap_global);
+  if (T < 1) return fail(SD_ERR_STATE, "decode on an empty cache");
+  if (x->cfg.top_k == 0) {
+    x->offset = T;
+    if (k_new) {
+      // Nothing to rank; still store the token on its owner shard.
+      return launch_decode(x, sd::MODE_CANDIDATES, int(T), q, k_new, v_new, scale, nullptr, nullptr, scores_out,
+                           cand_score, cand_block, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+    }
+    return SD_OK;
+  }
+  int32_t rc = launch_decode(x, sd::MODE_CANDIDATES, int(T), q, k_new, v_new, scale, nullptr, nullptr, scores_out,
+                             cand_score, cand_block, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+  if (rc == SD_OK) x->offset = T;
+  return rc;
+}
+
+int32_t sd_shard_attend(sd_index* x, const void* q, const float* all_cand_score, const int32_t* all_cand_block,
+                        float scale, float* part_ml, float* part_o, int32_t* sel_out, sd_stream stream) {
+  if (!x || !q || !part_ml || !part_o) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  if (x->cfg.top_k > 0 && (!all_cand_score || !all_cand_block)) return fail(SD_ERR_INVALID_ARG, "NULL candidates");
+  if (!std::isfinite(scale)) return fail(SD_ERR_INVALID_ARG, "scale must be finite");
+  if (x->offset < 1) return fail(SD_ERR_STATE, "attend on an empty cache");
+  return launch_decode(x, sd::MODE_ATTEND, int(x->offset), q, nullptr, nullptr, scale, nullptr, sel_out, nullptr,
+                       const_cast<float*>(all_cand_score), const_cast<int32_t*>(all_cand_block), part_ml, part_o,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int32_t sd_shard_merge(sd_index* x, const float* all_ml, const float* all_o, void* out, sd_stream stream) {
+  if (!x || !all_ml || !all_o || !out) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  const sd_config& c = x->cfg;
+  int P = c.shard_count, BQ = c.batch * c.n_q_heads, D = c.head_dim;
+  void* args[6] = {&P, &BQ, &D, const_cast<float**>(&all_ml), const_cast<float**>(&all_o), &out};
+  SD_CUDA(cudaLaunchKernel(x->ks.merge, dim3(unsigned(BQ)), dim3(128), args, 0, static_cast<cudaStream_t>(stream)));
+  return SD_OK;
+}
+
+int32_t sd_check_device(sd_index* x, int32_t* flags, sd_stream stream) {
+  if (!x || !flags) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int h = 0;
+  SD_CUDA(cudaMemcpyAsync(&h, x->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  SD_CUDA(cudaMemsetAsync(x->d_err, 0, sizeof(int), st));
+  SD_CUDA(cudaStreamSynchronize(st));
+  *flags = h;
+  return SD_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,339 @@
+// sd_device.cuh -- device-side building blocks for the sm_100a sparse decode
+// kernels: element conversion, PTX wrappers for mbarriers, TMA bulk copies and
+// thread-block clusters, CTA-wide scans and a radix select over 64-bit keys.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sd {
+
+// ---------------------------------------------------------------------------
+// Element types. A format is (E, BITS): E is the dense element type, or the
+// type of the per-group scales/biases when BITS is 4 or 8.
+// ---------------------------------------------------------------------------
+template <typename E> struct Elt;
+template <> struct Elt<float> {
+  static __device__ __forceinline__ float to_f32(float x) { return x; }
+  static __device__ __forceinline__ float from_f32(float x) { return x; }
+};
+template <> struct Elt<__half> {
+  static __device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from_f32(float x) { return __float2half_rn(x); }
+};
+template <> struct Elt<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f32(float x) { return __float2bfloat16_rn(x); }
+};
+
+// Unpack one 32-bit word holding 32/sizeof(E)/8 elements of E into floats.
+template <typename E> __device__ __forceinline__ void unpack_word(uint32_t w, float* f);
+template <> __device__ __forceinline__ void unpack_word<float>(uint32_t w, float* f) {
+  f[0] = __uint_as_float(w);
+}
+template <> __device__ __forceinline__ void unpack_word<__nv_bfloat16>(uint32_t w, float* f) {
+  f[0] = __uint_as_float(w << 16);
+  f[1] = __uint_as_float(w & 0xffff0000u);
+}
+template <> __device__ __forceinline__ void unpack_word<__half>(uint32_t w, float* f) {
+  __half2 h = *reinterpret_cast<__half2*>(&w);
+  float2 x = __half22float2(h);
+  f[0] = x.x;
+  f[1] = x.y;
+}
+
+// Byte-code -> float without an int->float conversion: 0x4B000000 | c is the
+// float 2^23 + c, exact for c < 2^23; subtracting 2^23 leaves c exactly.
+__device__ __forceinline__ float code_u8(uint32_t w, int i) {
+  return __uint_as_float(__byte_perm(w, 0x4Bu, 0x4550u + i)) - 8388608.0f;
+}
+__device__ __forceinline__ float code_u4(uint32_t w, int i) {
+  return __uint_as_float(((w >> (4 * i)) & 0xFu) | 0x4B000000u) - 8388608.0f;
+}
+
+// Order-preserving 32-bit key of a score (larger = better). NaN ranks lowest,
+// -0.0 is folded onto +0.0.
+__device__ __forceinline__ uint32_t score_key(float s) {
+  if (s != s) return 0u;
+  if (s == 0.0f) s = 0.0f;
+  uint32_t u = __float_as_uint(s);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_score(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+// Composite key: score first, then the lower block index wins. All distinct.
+__device__ __forceinline__ uint64_t full_key(uint32_t k32, int32_t j) {
+  return (uint64_t(k32) << 32) | uint64_t(0xffffffffu - uint32_t(j));
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory and global access helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float4 lds_f4(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+  return v;
+}
+// Streaming 16-byte global load that does not allocate in L1.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+// Byte offset inside a TMA box written with the 128B/64B/32B swizzle modes:
+// the 16-byte chunk index is XORed with address bits [7, 7+log2(cpb)).
+// Box bases are 1024-byte aligned, so offsets inside the box are enough.
+__device__ __forceinline__ uint32_t swz(uint32_t off, uint32_t cpb) {
+  return off ^ (((off >> 7) & (cpb - 1u)) << 4);
+}
+
+// ---------------------------------------------------------------------------
+// Time-bounded waiting. Every spin in these kernels gives up after this many
+// nanoseconds of %globaltimer, records an error and lets the kernel finish.
+// ---------------------------------------------------------------------------
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr int kErrTimeout = 1;
+constexpr int kErrBadIndex = 2;
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait on an mbarrier phase; false (and the error word set) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0u && globaltimer() - t0 > kWaitLimitNs) {
+      if (err) atomicOr(err, kErrTimeout);
+      return false;
+    }
+  }
+}
+
+// Generic-proxy writes -> async-proxy (TMA) reads ordering.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 2-D tiled TMA load of one box into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+// 1-D bulk copy global -> this CTA's shared memory (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Thread-block clusters
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t local_smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Warp / CTA reductions and scans
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Exclusive scan of one int per thread over the whole CTA (all threads call).
+// `scratch` holds at least 33 ints. Returns the exclusive prefix; *total gets the sum.
+__device__ __forceinline__ int cta_exclusive_scan(int v, int* scratch, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) scratch[lane] = w;  // inclusive warp totals
+    if (lane == 31) scratch[32] = w;
+  }
+  __syncthreads();
+  const int before = warp > 0 ? scratch[warp - 1] : 0;
+  *total = scratch[32];
+  const int r = before + x - v;
+  __syncthreads();
+  return r;
+}
+
+// State of a radix select, kept in shared memory.
+struct RadixState {
+  unsigned long long prefix;
+  unsigned long long mask;
+  int rem;
+  int digit;
+  int exact;
+  int pad;
+};
+
+// Radix select over n distinct 64-bit keys produced by keyf(i): finds
+// (prefix, mask) such that exactly k keys satisfy (key & mask) >= prefix,
+// i.e. the k largest keys. Requires 0 < k < n. All CTA threads call it.
+// hist: 256 u32 of shared memory.
+template <class KeyF>
+__device__ void radix_select(KeyF keyf, int n, int k, uint32_t* hist, RadixState* st) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+  unsigned long long prefix = 0ull, mask = 0ull;
+  int rem = k;
+  for (int pb = 7; pb >= 0; --pb) {
+    for (int i = tid; i < 256; i += nthr) hist[i] = 0u;
+    __syncthreads();
+    const int shift = 8 * pb;
+    for (int base = warp * 32; base < n; base += nthr) {
+      const int i = base + lane;
+      bool active = false;
+      uint32_t digit = 0;
+      if (i < n) {
+        const unsigned long long key = keyf(i);
+        active = (key & mask) == prefix;
+        digit = uint32_t(key >> shift) & 255u;
+      }
+      const unsigned amask = __ballot_sync(0xffffffffu, active);
+      if (active) {
+        const unsigned peers = __match_any_sync(amask, digit);
+        if (lane == __ffs(peers) - 1) atomicAdd(&hist[digit], uint32_t(__popc(peers)));
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l covers digits 255-8l .. 248-8l (descending)
+      uint32_t c[8];
+      uint32_t s = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) { c[e] = hist[255 - 8 * lane - e]; s += c[e]; }
+      uint32_t incl = s;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const uint32_t excl = incl - s;
+      if (excl < uint32_t(rem) && uint32_t(rem) <= incl) {
+        uint32_t above = excl;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (above + c[e] >= uint32_t(rem)) {
+            st->digit = 255 - 8 * lane - e;
+            st->rem = rem - int(above);
+            st->exact = (c[e] == uint32_t(rem) - above) ? 1 : 0;
+            break;
+          }
+          above += c[e];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= (unsigned long long)(st->digit) << shift;
+    mask |= 0xffull << shift;
+    rem = st->rem;
+    const bool done = st->exact != 0;
+    __syncthreads();
+    if (done) break;
+  }
+  if (tid == 0) { st->prefix = prefix; st->mask = mask; }
+  __syncthreads();
+}
+
+}  // namespace sd

@@ -1,0 +1,66 @@
+// sd_params.h -- kernel parameter blocks shared by the host launcher and the
+// device kernels. Plain C structs: pointers are device pointers.
+#pragma once
+
+#include <stdint.h>
+
+namespace sd {
+
+struct DecodeParams {
+  int B, Hq, Hkv, S, K;   // K = blocks chosen by top-K (the recent block is extra)
+  int T;                  // tokens in the sequence, after the optional append
+  int NB;                 // blocks = ceil(T / S)
+  int P, pr;              // sequence shards and this shard's rank (block j lives on j % P)
+  int cap_local;          // token rows per (b, kv-head) on this shard
+  int nb_stride;          // summary rows per (b, kv-head) on this shard
+  int C;                  // cluster size (CTAs per (b, kv-head))
+  int mode;               // sd::Mode
+  float scale;            // softmax scale applied to q.k
+  float scale_log2;       // scale * log2(e)
+  const void* q;          // [B, Hq, D]
+  const void* k_new;      // [B, Hkv, D] appended before attending, or null
+  const void* v_new;
+  void* k_data;           // dense [BH, cap_local, D] or codes [BH, cap_local, D*bits/32]
+  void* v_data;
+  void* k_scales;         // quantized only: [BH, cap_local, D/64]
+  void* k_biases;
+  void* v_scales;
+  void* v_biases;
+  void* summ;             // [BH, nb_stride, D] summary keys
+  void* out;              // [B, Hq, D] (fused mode)
+  int32_t* sel_out;       // [BH, K+1] or null: selected blocks, ascending, recent last, -1 padded
+  float* scores_out;      // [BH, NB] or null: block scores of this shard's blocks
+  float* cand_score;      // candidates mode: out [BH, K]; attend mode: in [P, BH, K]
+  int32_t* cand_block;
+  float* part_ml;         // attend mode: out [B*Hq, 2] = (max in log2 units, sum)
+  float* part_o;          // attend mode: out [B*Hq, D] unnormalised
+  int* err;               // device error word (sd::kErr*)
+};
+
+struct AppendParams {
+  int Hkv, S, P, pr;
+  int cap_local;
+  int n_tok;              // tokens in this append
+  int t0;                 // global position of the first appended token
+  const void* k_src;      // [B, Hkv, n_tok, D]
+  const void* v_src;
+  void* k_data;
+  void* v_data;
+  void* k_scales;
+  void* k_biases;
+  void* v_scales;
+  void* v_biases;
+};
+
+struct SummaryParams {
+  int Hkv, S, P, pr;
+  int cap_local, nb_stride;
+  int T;                  // tokens in the sequence
+  int jl0;                // first local block to rebuild (blockIdx.x offsets from here)
+  const void* k_data;
+  const void* k_scales;
+  const void* k_biases;
+  void* summ;
+};
+
+}  // namespace sd

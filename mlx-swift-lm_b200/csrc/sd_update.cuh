@@ -1,0 +1,141 @@
+// sd_update.cuh -- cache writes: appending token rows (with affine
+// quantization for 4/8-bit caches) and (re)building block summary keys.
+//
+// Storage follows the reference's KV layout [B, Hkv, cap, D]
+// (Libraries/MLXLMCommon/KVCache.swift:328-371) and its quantized tuple
+// (wq, scales, biases) with scales/biases in the key dtype
+// (KVCache.swift:816-889). With sequence sharding, block j of the sequence is
+// stored on shard j % P as local block j / P.
+#pragma once
+
+#include "sd_device.cuh"
+#include "sd_format.h"
+#include "sd_params.h"
+
+namespace sd {
+
+// Quantize one row of D elements (one warp) with the affine group-64 rule
+// (scale from the group's range, the larger-magnitude edge placed exactly on a
+// code, round-half-even codes clamped to [0, 2^bits-1], codes packed
+// little-endian in uint32 words). The fp32 operations match the CPU
+// restatement in oracle/sd_oracle.cpp (orc_quantize) one for one.
+template <typename E, int BITS, int D>
+__device__ __forceinline__ void quantize_row_warp(const E* src, uint32_t* wq, E* sc, E* bi, int lane) {
+  constexpr int EPL = D / 32;            // elements per lane
+  constexpr int LPG = 64 / EPL;          // lanes per quantization group
+  constexpr int PER_WORD = 32 / BITS;    // codes per uint32
+  constexpr int LPW = PER_WORD / EPL;    // lanes sharing one word (>= 1)
+  static_assert(EPL * BITS <= 32, "lane codes exceed one word");
+  const float n_bins = float((1 << BITS) - 1);
+  float w[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) w[e] = Elt<E>::to_f32(src[lane * EPL + e]);
+  float wmax = w[0], wmin = w[0];
+#pragma unroll
+  for (int e = 1; e < EPL; ++e) { wmax = fmaxf(wmax, w[e]); wmin = fminf(wmin, w[e]); }
+#pragma unroll
+  for (int o = 1; o < LPG; o <<= 1) {
+    wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+    wmin = fminf(wmin, __shfl_xor_sync(0xffffffffu, wmin, o));
+  }
+  float scale = fmaxf(__fdiv_rn(__fsub_rn(wmax, wmin), n_bins), 1e-7f);
+  const bool mask = fabsf(wmin) > fabsf(wmax);
+  if (!mask) scale = -scale;
+  const float edge = mask ? wmin : wmax;
+  const float q0 = rintf(__fdiv_rn(edge, scale));
+  if (q0 != 0.0f) scale = __fdiv_rn(edge, q0);
+  const float bias = (q0 == 0.0f) ? 0.0f : edge;
+  uint32_t bits = 0;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    float c = rintf(__fdiv_rn(__fsub_rn(w[e], bias), scale));
+    c = fminf(fmaxf(c, 0.0f), n_bins);
+    bits |= uint32_t(c) << (BITS * ((lane * EPL + e) % PER_WORD));
+  }
+#pragma unroll
+  for (int o = 1; o < LPW; o <<= 1) bits |= __shfl_xor_sync(0xffffffffu, bits, o);
+  if (lane % LPW == 0) wq[(lane * EPL) / PER_WORD] = bits;
+  if (lane % LPG == 0) {
+    const int g = (lane * EPL) / 64;
+    sc[g] = Elt<E>::from_f32(scale);
+    bi[g] = Elt<E>::from_f32(bias);
+  }
+}
+
+// Element d of key row `row` as fp32 (dequantized with fma(scale, code, bias)).
+template <typename E, int BITS, int D>
+__device__ __forceinline__ float load_key_elt(const void* data, const void* scales, const void* biases,
+                                              size_t row, int d) {
+  if constexpr (BITS == 0) {
+    return Elt<E>::to_f32(static_cast<const E*>(data)[row * D + d]);
+  } else {
+    constexpr int PER_WORD = 32 / BITS, WORDS = D / PER_WORD, NG = D / 64;
+    const uint32_t w = static_cast<const uint32_t*>(data)[row * WORDS + d / PER_WORD];
+    const float code = float((w >> (BITS * (d % PER_WORD))) & ((1u << BITS) - 1u));
+    const float s = Elt<E>::to_f32(static_cast<const E*>(scales)[row * NG + d / 64]);
+    const float b = Elt<E>::to_f32(static_cast<const E*>(biases)[row * NG + d / 64]);
+    return __fmaf_rn(s, code, b);
+  }
+}
+
+// Summary of one block: column mean over its n filled token rows starting at
+// `row0`, sequential fp32 adds in token order, IEEE division, rounded to E.
+// Threads [t0, t0 + nthr) of the caller cooperate over the D columns.
+template <typename E, int BITS, int D>
+__device__ __forceinline__ void block_summary(const void* data, const void* scales, const void* biases,
+                                              size_t row0, int n, E* dst, int t, int nthr) {
+  for (int d = t; d < D; d += nthr) {
+    float acc = load_key_elt<E, BITS, D>(data, scales, biases, row0, d);
+#pragma unroll 8
+    for (int i = 1; i < n; ++i) acc = __fadd_rn(acc, load_key_elt<E, BITS, D>(data, scales, biases, row0 + i, d));
+    dst[d] = Elt<E>::from_f32(__fdiv_rn(acc, float(n)));
+  }
+}
+
+// Write one token row of K and V (warp 0: K, warp 1: V) at local row `row`.
+template <typename E, int BITS, int D>
+__device__ __forceinline__ void write_token_row(const E* src, void* data, void* scales, void* biases,
+                                                size_t row, int lane) {
+  if constexpr (BITS == 0) {
+    E* dst = static_cast<E*>(data) + row * D;
+    for (int d = lane; d < D; d += 32) dst[d] = src[d];
+  } else {
+    constexpr int WORDS = D * BITS / 32, NG = D / 64;
+    quantize_row_warp<E, BITS, D>(src, static_cast<uint32_t*>(data) + row * WORDS,
+                                  static_cast<E*>(scales) + row * NG, static_cast<E*>(biases) + row * NG, lane);
+  }
+}
+
+// Append n_tok tokens [B, Hkv, n_tok, D] at global positions t0.. : one warp
+// per (token, K or V). Tokens whose block lives on another shard are skipped.
+template <typename E, int BITS, int D>
+__global__ void __launch_bounds__(256) append_kernel(const __grid_constant__ AppendParams p) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int i = blockIdx.x * 4 + (warp >> 1);
+  const int bh = blockIdx.y;
+  if (i >= p.n_tok) return;
+  const int t = p.t0 + i;
+  const int j = t / p.S;
+  if (j % p.P != p.pr) return;
+  const size_t row = size_t(bh) * p.cap_local + size_t(j / p.P) * p.S + (t % p.S);
+  const size_t src = (size_t(bh) * p.n_tok + i) * D;
+  if ((warp & 1) == 0)
+    write_token_row<E, BITS, D>(static_cast<const E*>(p.k_src) + src, p.k_data, p.k_scales, p.k_biases, row, lane);
+  else
+    write_token_row<E, BITS, D>(static_cast<const E*>(p.v_src) + src, p.v_data, p.v_scales, p.v_biases, row, lane);
+}
+
+// Rebuild the summaries of local blocks jl0 + blockIdx.x for every (b, kv-head).
+template <typename E, int BITS, int D>
+__global__ void __launch_bounds__(128) summary_kernel(const __grid_constant__ SummaryParams p) {
+  const int jl = p.jl0 + blockIdx.x;
+  const int bh = blockIdx.y;
+  const int j = jl * p.P + p.pr;
+  const int n = min(p.S, p.T - j * p.S);
+  if (n <= 0) return;
+  const size_t row0 = size_t(bh) * p.cap_local + size_t(jl) * p.S;
+  E* dst = static_cast<E*>(p.summ) + (size_t(bh) * p.nb_stride + jl) * D;
+  block_summary<E, BITS, D>(p.k_data, p.k_scales, p.k_biases, row0, n, dst, threadIdx.x, blockDim.x);
+}
+
+}  // namespace sd
