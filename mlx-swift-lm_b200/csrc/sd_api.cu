@@ -112,8 +112,8 @@ int32_t validate(const sd_config* c) {
   if (c->kv_bits != 0 && c->group_size != 64) return fail(SD_ERR_SHAPE, "group_size must be 64 for quantized caches (got %d)", c->group_size);
   if (c->shard_count < 1 || c->shard_count > 64) return fail(SD_ERR_INVALID_ARG, "shard_count must be in [1, 64]");
   if (c->shard_rank < 0 || c->shard_rank >= c->shard_count) return fail(SD_ERR_INVALID_ARG, "shard_rank out of range");
-  if (c->cluster_size < 0 || c->cluster_size > 16 || (c->cluster_size & (c->cluster_size - 1)) != 0)
-    return fail(SD_ERR_INVALID_ARG, "cluster_size must be 0 or a power of two <= 16");
+  if (c->cluster_size < 0 || c->cluster_size > 16)
+    return fail(SD_ERR_INVALID_ARG, "cluster_size must be in [0, 16]");
   for (int r : c->reserved)
     if (r != 0) return fail(SD_ERR_INVALID_ARG, "reserved config fields must be 0");
   if (c->shard_count * c->top_k > sd::kUnionMax)
@@ -164,36 +164,50 @@ int32_t setup_kernels(sd_index* x) {
   if (x->attrs_set) return SD_OK;
   SD_CUDA(cudaFuncSetAttribute(x->ks.decode, cudaFuncAttributeMaxDynamicSharedMemorySize, int(x->smem)));
   SD_CUDA(cudaFuncSetAttribute(x->ks.decode, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-  // An automatically chosen cluster that the device cannot co-schedule is
-  // halved; an explicitly requested one is an error.
-  while (max_active_clusters(x, x->C) < 1) {
-    if (x->cfg.cluster_size != 0 || x->C == 1)
-      return fail(SD_ERR_SHAPE, "cluster size %d cannot be scheduled with %zu bytes of shared memory", x->C, x->smem);
-    x->C /= 2;
-  }
   x->attrs_set = true;
   return SD_OK;
 }
 
-// Choose the cluster size: enough CTAs to cover the SMs once, capped by the
-// union buffer, and at least enough that one CTA scores <= kLocalKeysMax blocks.
-int choose_cluster(const sd_config& c, int64_t nb_local, int n_sm) {
+// Choose the cluster size (CTAs per (batch, kv-head)). Automatic choice: the
+// largest C <= 16 for which every group's cluster is resident at once (one
+// wave: a cluster must fit in one GPC, so with one CTA per SM a B200 holds 7
+// clusters of 16 but 8 of 10), with B*Hkv*C <= SMs, C*top_k within the union
+// buffer and at most kLocalKeysMax candidate blocks per CTA at full capacity.
+int32_t choose_cluster(sd_index* x) {
+  const sd_config& c = x->cfg;
   const int64_t BH = int64_t(c.batch) * c.n_kv_heads;
-  int C = c.cluster_size;
-  if (C == 0) {
-    C = 1;
-    while (C < 16 && BH * C * 2 <= n_sm) C *= 2;
+  int n_sm = 148;
+  cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, x->device);
+  auto fits = [&](int C) {
+    return int64_t(C) * c.top_k <= sd::kUnionMax && (x->nb_local + C - 1) / C <= sd::kLocalKeysMax;
+  };
+  if (c.cluster_size != 0) {
+    if (!fits(c.cluster_size))
+      return fail(SD_ERR_SHAPE, "cluster_size %d is too small for this capacity or top_k", c.cluster_size);
+    x->C = c.cluster_size;
+    if (max_active_clusters(x, x->C) < 1)
+      return fail(SD_ERR_SHAPE, "cluster size %d cannot be scheduled with %zu bytes of shared memory", x->C, x->smem);
+    return SD_OK;
   }
-  while (C > 1 && int64_t(C) * c.top_k > sd::kUnionMax) C /= 2;
-  while (C < 16 && (nb_local + C - 1) / C > sd::kLocalKeysMax) C *= 2;
-  return C;
+  for (int C = 16; C >= 1; --C) {
+    if (!fits(C) || BH * C > n_sm) continue;
+    if (max_active_clusters(x, C) >= BH) {
+      x->C = C;
+      return SD_OK;
+    }
+  }
+  // More groups than the GPU holds at once: the smallest feasible cluster.
+  for (int C = 1; C <= 16; ++C)
+    if (fits(C) && max_active_clusters(x, C) >= 1) {
+      x->C = C;
+      return SD_OK;
+    }
+  return fail(SD_ERR_SHAPE, "no schedulable cluster size for this configuration");
 }
 
 int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k_new, const void* v_new,
                       float scale, void* out, int32_t* sel_out, float* scores_out, float* cand_score,
                       int32_t* cand_block, float* part_ml, float* part_o, cudaStream_t st) {
-  int32_t rc = setup_kernels(x);
-  if (rc != SD_OK) return rc;
   const sd_config& c = x->cfg;
   sd::DecodeParams p{};
   p.B = c.batch; p.Hq = c.n_q_heads; p.Hkv = c.n_kv_heads; p.S = c.block_size; p.K = c.top_k;
@@ -308,11 +322,14 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
     delete x;
     return fail(SD_ERR_SHAPE, "no kernel for dtype %d, bits %d, head_dim %d, G %d", c.dtype, c.kv_bits, c.head_dim, x->G);
   }
-  int n_sm = 148;
-  cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, x->device);
-  x->C = choose_cluster(c, x->nb_local, n_sm);
   const sd::Layout L = sd::make_layout(c.head_dim, x->G, x->groups);
   x->smem = size_t(L.total) + 1024;
+  rc = setup_kernels(x);
+  if (rc == SD_OK) rc = choose_cluster(x);
+  if (rc != SD_OK) {
+    delete x;
+    return rc;
+  }
 
   const size_t kv = align256(size_t(BH) * x->cap_local * x->row_bytes);
   const size_t sb = c.kv_bits ? align256(size_t(BH) * x->cap_local * x->groups * x->esize) : 0;

@@ -2,26 +2,32 @@
 //
 // One thread-block cluster of C CTAs serves one (batch, kv-head) group:
 //   phase 0  queries of the group -> shared memory; optional append of the new
-//            token (the decode half of attentionWithCacheUpdate,
-//            Libraries/MLXLMCommon/AttentionUtils.swift:54-66 / :67-76).
-//   phase 1  score: every CTA scores its slice of the candidate blocks,
-//            score[j] = scale * (sum_g q_g) . summary[j], with half-warp /
-//            warp groups of 16-byte streaming loads (one chunk per lane) and a
-//            fixed fp32 reduction order (see oracle/sd_oracle.cpp).
-//   phase 2  select: per-CTA top-K by radix select on 64-bit keys
-//            (score, then lower block index), candidates pushed into every CTA
-//            of the cluster through distributed shared memory, then the
-//            group's top-K, ascending, plus the most recent block.
-//   phase 3  attend: selected blocks are cut into 32-token tiles, spread
+//            token (the cache.update half of attentionWithCacheUpdate,
+//            Libraries/MLXLMCommon/AttentionUtils.swift:54-66 / :67-76). The
+//            first summary loads are issued before the query barrier.
+//   phase 1  score: 8 warps of every CTA score its slice of the candidate
+//            blocks, score[j] = scale * (sum_g q_g) . summary[j], one 16-byte
+//            streaming load of the summary per lane and a fixed fp32
+//            reduction order (the CPU oracle restates it).
+//   phase 2  select: each CTA sorts its candidates in runs of 32 in registers
+//            (bitonic over shuffles) and ranks them by binary search into a
+//            descending top-K list; the lists are exchanged through
+//            distributed shared memory and every candidate's rank in the
+//            group is found the same way; selected = rank < K (ties: lower
+//            block index wins). Result: top-K ascending plus the recent block.
+//   phase 3  attend: the selected blocks are cut into 32-token tiles spread
 //            evenly over the cluster; a producer warp stages K and V tiles
 //            with TMA (128B/64B/32B swizzle, no multicast) into a ring of
-//            mbarrier-guarded stages; 8 consumer warps run online softmax
-//            (exp2 domain) with 4/8-bit codes dequantized in registers.
-//   phase 4  merge: warp partials -> CTA partial -> cluster-wide log-sum-exp
-//            merge over DSMEM, each CTA writing a slice of the output.
+//            mbarrier-guarded stages; 8 consumer warps run online softmax in
+//            the exp2 domain -- on tensor cores (mma.sync m16n8k16) for
+//            16-bit K/V, on FMA pipes with 4/8-bit codes dequantized in
+//            registers otherwise.
+//   phase 4  merge: warp partials -> CTA partial -> every CTA pushes its
+//            partial to the CTA owning each output slice (DSMEM), one cluster
+//            barrier, log-sum-exp merge from local shared memory.
 // Sharded decode (MODE_CANDIDATES / MODE_ATTEND) runs phases 0-2 and 2-4 as
 // two launches around the caller's all-gather of candidates.
-// Semantics of stage 4 follow quantizedScaledDotProductAttention
+// Stage-4 semantics follow quantizedScaledDotProductAttention
 // (Libraries/MLXLMCommon/KVCache.swift:1544-1618) restricted to the gathered
 // tokens.
 #pragma once
@@ -47,6 +53,338 @@ __device__ __forceinline__ int cta_compact(int n, Pred pred, Emit emit, int* scr
     if (pred(i)) emit(pos++, i);
   __syncthreads();
   return total;
+}
+
+// What a consumer warp needs to walk its tiles.
+struct TileWalk {
+  uint8_t* ring;       // stage s at ring + s * stage bytes
+  uint64_t* full;
+  uint64_t* empty;
+  const int* own;      // selected blocks of this shard, recent last
+  int u0, nmine, tpb;  // this CTA's units [u0, u0 + nmine), tiles per block
+  float* mw;           // per-warp partial slots (m[G], l[G], o[G][D])
+};
+
+// FMA consumer (fp32 K/V, or 4/8-bit codes). Lane = token row for q.k; for
+// p.v each lane owns kPiece bytes (kDpl head dims) of a row.
+template <typename E, int BITS, int D, int G>
+__device__ __forceinline__ void consume_tiles_fma(const DecodeParams& p, const TileWalk& tw, const float* qf,
+                                                  const float* qs, float* ps, int warp, int lane) {
+  using F = Fmt<int(sizeof(E)), BITS, D>;
+  constexpr int NG = F::kGroups, TS = kTileTokens;
+  const int S = p.S, T = p.T;
+  float m_run[G], l_run[G], o_acc[G][F::kDpl], ob[G][NG];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m_run[g] = -INFINITY;
+    l_run[g] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] = 0.0f;
+#pragma unroll
+    for (int r = 0; r < NG; ++r) ob[g][r] = 0.0f;
+  }
+  const uint32_t ps_a = smem_u32(ps);
+  const uint32_t qf_a = smem_u32(qf);
+  for (int i = warp; i < tw.nmine; i += kConsumerWarps) {
+    const int s = i % F::kStages;
+    if (mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
+      const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
+      const int nv = min(TS, T - (j * S + tile * TS));
+      uint8_t* stage = tw.ring + s * F::kStageBytes;
+      const uint32_t kb = smem_u32(stage);
+      const uint32_t vb = kb + F::kKvTileBytes;
+      // --- q.k: lane = token row ---
+      const int t = lane;
+      float sc[G], acc[G][NG];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        sc[g] = 0.0f;
+#pragma unroll
+        for (int r = 0; r < NG; ++r) acc[g][r] = 0.0f;
+      }
+#pragma unroll
+      for (int ch = 0; ch < F::kNChunk; ++ch) {
+        const int bx = ch / F::kCpb, cc = ch % F::kCpb;
+        const uint4 raw = lds128(kb + bx * TS * F::kBoxBytes + swz(uint32_t(t * F::kBoxBytes + cc * 16), F::kCpb));
+        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          constexpr int EPW = F::kEpc / 4;  // elements per 32-bit word
+          float f[EPW];
+          if constexpr (BITS == 8) {
+#pragma unroll
+            for (int e = 0; e < EPW; ++e) f[e] = code_u8(wv[wi], e);
+          } else if constexpr (BITS == 4) {
+#pragma unroll
+            for (int e = 0; e < EPW; ++e) f[e] = code_u4(wv[wi], e);
+          } else {
+            unpack_word<E>(wv[wi], f);
+          }
+#pragma unroll
+          for (int e = 0; e < EPW; ++e) {
+            const int d = ch * F::kEpc + wi * EPW + e;
+            float qv[G];
+            if constexpr (G % 4 == 0) {
+#pragma unroll
+              for (int g4 = 0; g4 < G; g4 += 4) {
+                const float4 x = lds_f4(qf_a + (d * G + g4) * 4);
+                qv[g4] = x.x; qv[g4 + 1] = x.y; qv[g4 + 2] = x.z; qv[g4 + 3] = x.w;
+              }
+            } else {
+#pragma unroll
+              for (int g = 0; g < G; ++g) qv[g] = qf[d * G + g];
+            }
+            if constexpr (BITS == 0) {
+#pragma unroll
+              for (int g = 0; g < G; ++g) sc[g] = fmaf(qv[g], f[e], sc[g]);
+            } else {
+              const int grp = d / 64;
+#pragma unroll
+              for (int g = 0; g < G; ++g) acc[g][grp] = fmaf(qv[g], f[e], acc[g][grp]);
+            }
+          }
+        }
+      }
+      float vsc[NG], vbi[NG];
+      if constexpr (BITS != 0) {
+        const E* ksc = reinterpret_cast<const E*>(stage + 2 * F::kKvTileBytes);
+        const E* kbi = ksc + TS * NG;
+        const E* vs = ksc + 2 * TS * NG;
+        const E* vbp = ksc + 3 * TS * NG;
+#pragma unroll
+        for (int r = 0; r < NG; ++r) {
+          const float s_ = Elt<E>::to_f32(ksc[t * NG + r]);
+          const float b_ = Elt<E>::to_f32(kbi[t * NG + r]);
+#pragma unroll
+          for (int g = 0; g < G; ++g) sc[g] = fmaf(s_, acc[g][r], fmaf(b_, qs[g * NG + r], sc[g]));
+          vsc[r] = Elt<E>::to_f32(vs[t * NG + r]);
+          vbi[r] = Elt<E>::to_f32(vbp[t * NG + r]);
+        }
+      }
+      // --- online softmax over the tile (log2 domain) ---
+      const bool valid = t < nv;
+      float pv[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float s_ = valid ? sc[g] : -INFINITY;
+        const float mx = warp_max(s_);
+        const float mn = fmaxf(m_run[g], mx);
+        const float alpha = exp2f(m_run[g] - mn);
+        pv[g] = valid ? exp2f(s_ - mn) : 0.0f;
+        l_run[g] = l_run[g] * alpha + warp_sum(pv[g]);
+#pragma unroll
+        for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] *= alpha;
+        m_run[g] = mn;
+        if constexpr (BITS != 0) {
+#pragma unroll
+          for (int r = 0; r < NG; ++r) ob[g][r] = ob[g][r] * alpha + warp_sum(valid ? pv[g] * vbi[r] : 0.0f);
+        }
+      }
+      if constexpr (BITS == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) ps[t * G + g] = pv[g];
+      } else {
+#pragma unroll
+        for (int r = 0; r < NG; ++r)
+#pragma unroll
+          for (int g = 0; g < G; ++g) ps[(t * NG + r) * G + g] = pv[g] * vsc[r];
+      }
+      __syncwarp();
+      // --- p.v: lane owns kPiece bytes (kDpl dims) of rows rr, rr + kRpp, ... ---
+      const int rr = lane / F::kLpr, pi = lane % F::kLpr;
+      const int byte0 = pi * F::kPiece;
+      const int chunk = byte0 / 16, within = byte0 % 16;
+      const int bx = chunk / F::kCpb, cc = chunk % F::kCpb;
+      const int grp = (pi * F::kDpl) / 64;
+      for (int r = rr; r < nv; r += F::kRpp) {
+        float pg[G];
+        const uint32_t pa = ps_a + ((BITS == 0 ? r : r * NG + grp) * G) * 4;
+        if constexpr (G % 4 == 0) {
+#pragma unroll
+          for (int g4 = 0; g4 < G; g4 += 4) {
+            const float4 x = lds_f4(pa + g4 * 4);
+            pg[g4] = x.x; pg[g4 + 1] = x.y; pg[g4 + 2] = x.z; pg[g4 + 3] = x.w;
+          }
+        } else {
+#pragma unroll
+          for (int g = 0; g < G; ++g) pg[g] = ps[(BITS == 0 ? r : r * NG + grp) * G + g];
+        }
+        const uint32_t va = vb + bx * TS * F::kBoxBytes + swz(uint32_t(r * F::kBoxBytes + cc * 16), F::kCpb) + within;
+        float v[F::kDpl];
+        if constexpr (F::kPiece == 16) {
+          const uint4 x = lds128(va);
+          unpack_word<E>(x.x, v);
+          unpack_word<E>(x.y, v + F::kDpl / 4);
+          unpack_word<E>(x.z, v + F::kDpl / 2);
+          unpack_word<E>(x.w, v + 3 * F::kDpl / 4);
+        } else if constexpr (F::kPiece == 8) {
+          const uint2 x = lds64(va);
+          unpack_word<E>(x.x, v);
+          unpack_word<E>(x.y, v + F::kDpl / 2);
+        } else {
+          const uint32_t x = lds32(va);
+          if constexpr (BITS == 8) {
+#pragma unroll
+            for (int e = 0; e < F::kDpl; ++e) v[e] = code_u8(x, e);
+          } else if constexpr (BITS == 4) {
+#pragma unroll
+            for (int e = 0; e < F::kDpl; ++e) v[e] = code_u4(x, e);
+          } else {
+            unpack_word<E>(x, v);
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+          for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] = fmaf(pg[g], v[e], o_acc[g][e]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tw.empty + s);
+  }
+  // Fold the row groups of the p.v mapping together.
+#pragma unroll
+  for (int o = F::kLpr; o < 32; o <<= 1)
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] += __shfl_xor_sync(0xffffffffu, o_acc[g][e], o);
+  if constexpr (BITS != 0) {
+    const int grp = ((lane % F::kLpr) * F::kDpl) / 64;
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] += ob[g][grp];
+  }
+  named_barrier(1, kConsumerWarps * 32);  // all consumers are done with the ring
+  float* w = tw.mw + warp * (G * D + 2 * G);
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) { w[g] = m_run[g]; w[G + g] = l_run[g]; }
+  }
+  if (lane < F::kLpr) {
+    const int d0 = lane * F::kDpl;
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int e = 0; e < F::kDpl; ++e) w[2 * G + g * D + d0 + e] = o_acc[g][e];
+  }
+}
+
+// Tensor-core consumer for 16-bit dense K/V. Rows of the m16n8k16 tiles are
+// the G query heads of the group (rows >= G are zero); columns are tokens
+// (q.k^T) or head dims (p.v).
+//   q.k^T: A = q (registers, loaded once), B = K rows through ldmatrix from
+//          the 128B-swizzled tile; fp32 accumulation, then * scale*log2(e).
+//   softmax: per head over the tile (exp2 domain), running (m, l) per lane.
+//   p.v:   A = P taken from the q.k^T accumulators (the C fragment of two
+//          8-token column tiles is the A fragment of one 16-token k-step),
+//          split into hi + lo 16-bit halves so the weights keep ~16
+//          significant bits; B = V rows through ldmatrix.trans.
+template <typename E, int D, int G>
+__device__ __forceinline__ void consume_tiles_mma(const DecodeParams& p, const TileWalk& tw, const E* qg, int warp,
+                                                  int lane) {
+  using F = Fmt<2, 0, D>;
+  constexpr int TS = kTileTokens, KSTEPS = D / 16, NT = TS / 8, ND = D / 8;
+  const int g = lane >> 2, tq = lane & 3;
+  const int S = p.S, T = p.T;
+  uint32_t qa0[KSTEPS], qa2[KSTEPS];
+  {
+    const uint32_t* qw = reinterpret_cast<const uint32_t*>(qg + size_t(g < G ? g : 0) * D);
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) {
+      qa0[ks] = g < G ? qw[8 * ks + tq] : 0u;
+      qa2[ks] = g < G ? qw[8 * ks + 4 + tq] : 0u;
+    }
+  }
+  float m_run = -INFINITY, l_run = 0.0f;
+  float o[ND][4];
+#pragma unroll
+  for (int nd = 0; nd < ND; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.0f;
+  const int mq = lane >> 3, r8 = lane & 7;
+  for (int i = warp; i < tw.nmine; i += kConsumerWarps) {
+    const int s = i % F::kStages;
+    if (mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
+      const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
+      const int nv = min(TS, T - (j * S + tile * TS));
+      const uint32_t kb = smem_u32(tw.ring + s * F::kStageBytes);
+      const uint32_t vb = kb + F::kKvTileBytes;
+      float sc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+#pragma unroll
+        for (int kp = 0; kp < KSTEPS / 2; ++kp) {
+          const int chunk = 4 * kp + mq, bx = chunk >> 3, cc = chunk & 7;
+          const int row = 8 * nt + r8;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kb + bx * TS * 128 + swz(uint32_t(row * 128 + cc * 16), 8u), b0, b1, b2, b3);
+          mma16816<E>(sc[nt], qa0[2 * kp], qa2[2 * kp], b0, b1);
+          mma16816<E>(sc[nt], qa0[2 * kp + 1], qa2[2 * kp + 1], b2, b3);
+        }
+      }
+      // online softmax over the tile per head (lanes 4g..4g+3 share head g)
+      float mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = 8 * nt + 2 * tq + e;
+          sc[nt][e] = t < nv ? sc[nt][e] * p.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, sc[nt][e]);
+        }
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m_run, mx);
+      const float alpha = exp2f(m_run - mn);
+      float rs = 0.0f;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          sc[nt][e] = exp2f(sc[nt][e] - mn);  // exp2(-inf) = 0 for padding tokens
+          rs += sc[nt][e];
+        }
+      }
+      rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+      rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+      l_run = l_run * alpha + rs;
+      m_run = mn;
+#pragma unroll
+      for (int nd = 0; nd < ND; ++nd) { o[nd][0] *= alpha; o[nd][1] *= alpha; }
+      // p.v: two k-steps of 16 tokens
+#pragma unroll
+      for (int kt = 0; kt < NT / 2; ++kt) {
+        uint32_t h0, l0, h2, l2;
+        split2<E>(sc[2 * kt][0], sc[2 * kt][1], h0, l0);
+        split2<E>(sc[2 * kt + 1][0], sc[2 * kt + 1][1], h2, l2);
+        const int tok = 16 * kt + r8 + 8 * (mq & 1);
+#pragma unroll
+        for (int dp = 0; dp < ND / 2; ++dp) {
+          const int chunk = 2 * dp + (mq >> 1), bx = chunk >> 3, cc = chunk & 7;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vb + bx * TS * 128 + swz(uint32_t(tok * 128 + cc * 16), 8u), b0, b1, b2, b3);
+          mma16816<E>(o[2 * dp], h0, h2, b0, b1);
+          mma16816<E>(o[2 * dp], l0, l2, b0, b1);
+          mma16816<E>(o[2 * dp + 1], h0, h2, b2, b3);
+          mma16816<E>(o[2 * dp + 1], l0, l2, b2, b3);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tw.empty + s);
+  }
+  named_barrier(1, kConsumerWarps * 32);  // all consumers are done with the ring
+  float* w = tw.mw + warp * (G * D + 2 * G);
+  if (g < G) {
+    if (tq == 0) { w[g] = m_run; w[G + g] = l_run; }
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd) {
+      w[2 * G + g * D + 8 * nd + 2 * tq] = o[nd][0];
+      w[2 * G + g * D + 8 * nd + 2 * tq + 1] = o[nd][1];
+    }
+  }
 }
 
 template <typename E, int BITS, int D, int G>
@@ -75,15 +413,54 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   RadixState* rs = reinterpret_cast<RadixState*>(scratch + 40);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bars);
   uint64_t* empty = full + 16;
+  // Ring aliases (only one is live at a time): candidate keys [0, 64K);
+  // sorted runs [64K, 72K); radix-reduced candidates [72K, 80K); the
+  // cluster's sorted lists [80K, 144K); selection flags [144K, 152K); the
+  // selection result over the keys; sharded-attend union [64K, 128K).
   uint32_t* keys = reinterpret_cast<uint32_t*>(sm + L.ring);
   uint2* uni = reinterpret_cast<uint2*>(sm + L.ring + L.union_off);
-  uint2* pick = reinterpret_cast<uint2*>(sm + L.ring);  // selection result (keys are dead by then)
+  uint2* pick = reinterpret_cast<uint2*>(sm + L.ring);
 
   // ---------------- phase 0: barriers, queries, append ----------------
   if (tid == 0) {
     for (int s = 0; s < F::kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     fence_mbar_init();
   }
+  if (warp == kConsumerWarps && lane == 0 && p.mode != MODE_CANDIDATES) {
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+  }
+  const bool owner_recent = ((NB - 1) % P) == pr;
+  const bool appending = p.k_new != nullptr && p.mode != MODE_ATTEND && owner_recent && crank == C - 1;
+  // The appended token fills its block: the block's summary is computed in
+  // this launch (after the barrier that publishes the appended row), split by
+  // columns over the cluster's CTAs.
+  const bool completing = p.k_new != nullptr && p.mode != MODE_ATTEND && owner_recent && (T % S) == 0;
+
+  const int ncand = NB - 1;  // candidate blocks [0, NB-1); the recent block is always taken
+  const int nloc = ncand > pr ? (ncand - pr + P - 1) / P : 0;
+  // 32-bit: r * nloc <= 16 * 2^19 (the host bounds capacity and cluster size)
+  auto chunk_lo = [&](int r) { return r * nloc / C; };
+  const int c0 = chunk_lo(crank), c1 = chunk_lo(crank + 1);
+  const int n = c1 - c0;
+  auto jglob = [&](int i) { return (c0 + i) * P + pr; };
+
+  // Score-phase loads go out before the query barrier so that the two memory
+  // latencies overlap. Warps 0..7 score; the producer warp does not.
+  constexpr int LPB = F::kSumLanes, EPC = F::kSumEpc, BPW = 32 / LPB, UNR = 4, NWS = kConsumerWarps;
+  const int sub = lane / LPB, cch = lane % LPB;
+  const bool scorer = warp < NWS && p.mode != MODE_ATTEND;
+  const uint8_t* srow0 =
+      static_cast<const uint8_t*>(p.summ) + (size_t(bh) * p.nb_stride + c0) * D * sizeof(E) + cch * 16;
+  uint4 raw[UNR];
+  if (scorer) {
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const int i = warp * BPW + u * NWS * BPW + sub;
+      raw[u] = i < n ? ldg_stream(srow0 + size_t(i) * D * sizeof(E)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+
   const E* qg = static_cast<const E*>(p.q) + (size_t(b) * p.Hq + size_t(h) * G) * D;
   for (int i = tid; i < G * D; i += kThreads) {
     const int g = i / D, d = i % D;
@@ -95,8 +472,6 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     for (int g = 1; g < G; ++g) a = __fadd_rn(a, Elt<E>::to_f32(qg[g * D + tid]));
     qsum[tid] = a;
   }
-  const bool owner_recent = ((NB - 1) % P) == pr;
-  const bool appending = p.k_new != nullptr && p.mode != MODE_ATTEND && owner_recent && crank == C - 1;
   if (appending && warp < 2) {
     const int t = T - 1;
     const size_t row = size_t(bh) * p.cap_local + size_t((NB - 1) / P) * S + (t % S);
@@ -119,41 +494,36 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   }
 
   // ---------------- phase 1: block scores ----------------
-  const int ncand = NB - 1;  // candidate blocks [0, NB-1); the recent block is always taken
-  const int nloc = ncand > pr ? (ncand - pr + P - 1) / P : 0;
-  auto chunk_lo = [&](int r) { return int((long long)r * nloc / C); };
-  const int c0 = chunk_lo(crank), c1 = chunk_lo(crank + 1);
-  const int n = c1 - c0;
-  if (p.mode != MODE_ATTEND) {
-    constexpr int LPB = F::kSumLanes, EPC = F::kSumEpc, BPW = 32 / LPB, U = 4;
-    constexpr int NW = kThreads / 32;
-    const int sub = lane / LPB, c = lane % LPB;
+  if (scorer) {
     float qr[EPC];
 #pragma unroll
-    for (int e = 0; e < EPC; ++e) qr[e] = qsum[c * EPC + e];
-    const uint8_t* srow0 =
-        static_cast<const uint8_t*>(p.summ) + (size_t(bh) * p.nb_stride + c0) * D * sizeof(E) + c * 16;
-    for (int it = warp * BPW; it < n; it += NW * BPW * U) {
-      uint4 raw[U];
+    for (int e = 0; e < EPC; ++e) qr[e] = qsum[cch * EPC + e];
+    for (int it = warp * BPW; it < n; it += NWS * BPW * UNR) {
+      uint4 cur[UNR];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int i = it + u * NW * BPW + sub;
-        raw[u] = i < n ? ldg_stream(srow0 + size_t(i) * D * sizeof(E)) : make_uint4(0u, 0u, 0u, 0u);
+      for (int u = 0; u < UNR; ++u) cur[u] = raw[u];
+      const int nx = it + NWS * BPW * UNR;
+      if (nx < n) {
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+          const int i = nx + u * NWS * BPW + sub;
+          raw[u] = i < n ? ldg_stream(srow0 + size_t(i) * D * sizeof(E)) : make_uint4(0u, 0u, 0u, 0u);
+        }
       }
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int i = it + u * NW * BPW + sub;
+      for (int u = 0; u < UNR; ++u) {
+        const int i = it + u * NWS * BPW + sub;
         float f[EPC];
-        unpack_word<E>(raw[u].x, f);
-        unpack_word<E>(raw[u].y, f + EPC / 4);
-        unpack_word<E>(raw[u].z, f + EPC / 2);
-        unpack_word<E>(raw[u].w, f + 3 * EPC / 4);
+        unpack_word<E>(cur[u].x, f);
+        unpack_word<E>(cur[u].y, f + EPC / 4);
+        unpack_word<E>(cur[u].z, f + EPC / 2);
+        unpack_word<E>(cur[u].w, f + 3 * EPC / 4);
         float a = 0.0f;
 #pragma unroll
         for (int e = 0; e < EPC; ++e) a = __fmaf_rn(qr[e], f[e], a);
 #pragma unroll
         for (int o = LPB / 2; o >= 1; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-        if (c == 0 && i < n) {
+        if (cch == 0 && i < n) {
           const float sc = __fmul_rn(a, p.scale);
           keys[i] = score_key(sc);
           if (p.scores_out) p.scores_out[size_t(bh) * NB + size_t(c0 + i) * P + pr] = sc;
@@ -164,49 +534,119 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   __syncthreads();
 
   // ---------------- phase 2: selection ----------------
-  int U = 0;  // entries in the union
+  int kk;  // blocks chosen by top-K
   if (p.mode != MODE_ATTEND) {
-    int my_off = 0;
-    for (int r = 0; r < C; ++r) {
-      const int cr = min(K, chunk_lo(r + 1) - chunk_lo(r));
-      if (r < crank) my_off += cr;
-      U += cr;
-    }
-    auto jglob = [&](int i) { return (c0 + i) * P + pr; };
-    auto put = [&](int pos, int i) {
-      const uint32_t k32 = keys[i];
-      const int32_t j = jglob(i);
-      if (C == 1) {
-        uni[my_off + pos] = make_uint2(k32, uint32_t(j));
-      } else {
-        const uint32_t a = smem_u32(&uni[my_off + pos]);
-        for (int r = 0; r < C; ++r) st_cluster_v2(map_rank(a, uint32_t(r)), k32, uint32_t(j));
+    // (1) This CTA's candidates (its top-K by radix select first when it holds
+    // more than kRunMax) are sorted in runs of 32 in registers and ranked
+    // against each other by binary search: this CTA's top-K, descending.
+    // (2) The lists are exchanged through DSMEM. (3) A candidate's rank in the
+    // group is its position in its own list plus the number of larger keys in
+    // every other list; selected = rank < K. The selected entries of a list
+    // are a prefix of it, so the ascending block order follows from per-list
+    // counts alone.
+    constexpr int kRunMax = 1024;
+    unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 64 * 1024);
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(sm + L.ring + 72 * 1024);
+    unsigned long long* lists = reinterpret_cast<unsigned long long*>(sm + L.ring + 80 * 1024);
+    uint8_t* flag = sm + L.ring + 144 * 1024;
+    int* llen = scratch + 64;   // per-rank list length
+    int* lbase = scratch + 80;  // per-rank offset in the union
+    int* cnt = scratch + 96;    // per-rank selected count
+    if (tid == 0) {
+      int acc = 0, kmax = 0;
+      for (int r = 0; r < C; ++r) {
+        llen[r] = min(K, chunk_lo(r + 1) - chunk_lo(r));
+        lbase[r] = acc;
+        acc += llen[r];
+        kmax = max(kmax, llen[r]);
       }
-    };
-    if (K > 0 && n > K) {
-      auto keyf = [&](int i) -> unsigned long long { return full_key(keys[i], jglob(i)); };
+      scratch[112] = acc;   // U: union size
+      scratch[113] = kmax;  // list slot stride
+    }
+    if (tid < C) cnt[tid] = 0;
+    auto keyf = [&](int i) -> unsigned long long { return full_key(keys[i], jglob(i)); };
+    int nsrc = n;
+    bool from_cand = false;
+    if (K > 0 && n > kRunMax) {
       radix_select(keyf, n, K, hist, rs);
       const unsigned long long pre = rs->prefix, msk = rs->mask;
-      cta_compact(n, [&](int i) { return (keyf(i) & msk) >= pre; }, put, scratch);
-    } else if (K > 0) {
-      for (int i = tid; i < n; i += kThreads) put(i, i);
+      cta_compact(n, [&](int i) { return (keyf(i) & msk) >= pre; }, [&](int pos, int i) { cand[pos] = keyf(i); },
+                  scratch);
+      nsrc = K;
+      from_cand = true;
     }
-    if (C > 1) cluster_sync(); else __syncthreads();
+    __syncthreads();
+    const int U = scratch[112];
+    const int KS = max(scratch[113], 1);
+    const int kr = min(K, nsrc);
+    unsigned long long* mine = lists + crank * KS;
+    if (kr > 0) {
+      const int nrun = (nsrc + 31) / 32;
+      for (int rr = warp; rr < nrun; rr += kThreads / 32) {
+        const int i = rr * 32 + lane;
+        unsigned long long x = 0ull;
+        if (i < nsrc) x = from_cand ? cand[i] : keyf(i);
+        runs[rr * 32 + lane] = warp_sort_desc(x, lane);
+      }
+      __syncthreads();
+      for (int i = tid; i < nsrc; i += kThreads) {
+        const unsigned long long x = runs[i];
+        const int ra = i >> 5;
+        int rank = i & 31;
+        for (int rb = 0; rb < nrun; ++rb)
+          if (rb != ra) rank += count_greater(runs + rb * 32, min(32, nsrc - rb * 32), x);
+        if (rank < kr) mine[rank] = x;
+      }
+    }
+    __syncthreads();
+    if (C > 1) {
+      const uint32_t la = smem_u32(mine);
+      for (int pidx = tid; pidx < kr * C; pidx += kThreads) {
+        const int r = pidx / kr, i = pidx - r * kr;
+        if (r == crank) continue;
+        const unsigned long long x = mine[i];
+        st_cluster_v2(map_rank(la + i * 8, uint32_t(r)), uint32_t(x), uint32_t(x >> 32));
+      }
+      cluster_sync();
+    }
+    for (int u = tid; u < U; u += kThreads) {
+      int r = 0;
+      while (r + 1 < C && u >= lbase[r + 1]) ++r;
+      const int i = u - lbase[r];
+      const unsigned long long x = lists[r * KS + i];
+      int rank = i;
+      for (int r2 = 0; r2 < C; ++r2)
+        if (r2 != r) rank += count_greater(lists + r2 * KS, llen[r2], x);
+      const bool selected = rank < K;
+      flag[u] = selected ? 1 : 0;
+      if (selected) atomicAdd(&cnt[r], 1);
+    }
+    __syncthreads();
+    kk = min(K, U);
+    for (int u = tid; u < U; u += kThreads) {
+      if (!flag[u]) continue;
+      int r = 0, before = 0;
+      while (r + 1 < C && u >= lbase[r + 1]) { before += cnt[r]; ++r; }
+      const unsigned long long x = lists[r * KS + (u - lbase[r])];
+      const uint32_t jx = 0xffffffffu - uint32_t(x);
+      int pos = before;
+      for (int i2 = 0; i2 < cnt[r]; ++i2) pos += (0xffffffffu - uint32_t(lists[r * KS + i2])) < jx ? 1 : 0;
+      pick[pos] = make_uint2(uint32_t(x >> 32), jx);
+    }
+    __syncthreads();
   } else {
-    // Sharded attend: gather the P shards' candidates, dropping padding.
+    // Sharded attend: the P shards' candidates (gathered by the caller),
+    // padding dropped, then the group's top-K by radix select.
     const int tot = P * K;
     const size_t BH = size_t(gridDim.y);
     auto src = [&](int i) { return (size_t(i / K) * BH + bh) * K + (i % K); };
-    U = cta_compact(
+    const int U = cta_compact(
         tot, [&](int i) { return p.cand_block[src(i)] >= 0; },
         [&](int pos, int i) {
           uni[pos] = make_uint2(score_key(p.cand_score[src(i)]), uint32_t(p.cand_block[src(i)]));
         },
         scratch);
-  }
-
-  const int kk = min(K, U);
-  {
+    kk = min(K, U);
     auto ukey = [&](int i) -> unsigned long long { return full_key(uni[i].x, int32_t(uni[i].y)); };
     if (U > K && K > 0) {
       radix_select(ukey, U, K, hist, rs);
@@ -219,18 +659,31 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     }
   }
 
+  // The completed block's summary (its last row is the appended one,
+  // published by the barrier above), columns split over the cluster; run by
+  // the producer warp.
+  constexpr int SCOLS = (D + 31) / 32;
+  auto finish_summary = [&]() {
+    const int sc0 = crank * D / C, sc1 = (crank + 1) * D / C;
+    const size_t crow0 = size_t(bh) * p.cap_local + size_t((NB - 1) / P) * S;
+    E* dst = static_cast<E*>(p.summ) + (size_t(bh) * p.nb_stride + (NB - 1) / P) * D;
+#pragma unroll
+    for (int k = 0; k < SCOLS; ++k) {
+      const int d = sc0 + lane + 32 * k;
+      if (d < sc1)
+        dst[d] = Elt<E>::from_f32(
+            __fdiv_rn(column_sum<E, BITS, D>(p.k_data, p.k_scales, p.k_biases, crow0, S, d), float(S)));
+    }
+  };
+
   if (p.mode == MODE_CANDIDATES) {
+    if (completing && warp == kConsumerWarps) finish_summary();
     if (crank == 0) {
       for (int i = tid; i < K; i += kThreads) {
         const bool v = i < kk;
         p.cand_score[size_t(bh) * K + i] = v ? key_score(pick[i].x) : -INFINITY;
         p.cand_block[size_t(bh) * K + i] = v ? int32_t(pick[i].y) : -1;
       }
-    }
-    if (appending && warp == 0 && (T % S) == 0) {
-      const size_t row0 = size_t(bh) * p.cap_local + size_t((NB - 1) / P) * S;
-      E* dst = static_cast<E*>(p.summ) + (size_t(bh) * p.nb_stride + (NB - 1) / P) * D;
-      block_summary<E, BITS, D>(p.k_data, p.k_scales, p.k_biases, row0, S, dst, lane, 32);
     }
     return;
   }
@@ -268,254 +721,61 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   const int tpb = S / TS;
   const int recent_tiles = (T - (NB - 1) * S + TS - 1) / TS;
   const int n_units = owner_recent ? (nown - 1) * tpb + recent_tiles : nown * tpb;
-  const int u0 = int((long long)crank * n_units / C), u1 = int((long long)(crank + 1) * n_units / C);
+  const int u0 = crank * n_units / C, u1 = (crank + 1) * n_units / C;
   const int nmine = u1 - u0;
-
-  float m_run[G], l_run[G], o_acc[G][F::kDpl], ob[G][NG];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m_run[g] = -INFINITY;
-    l_run[g] = 0.0f;
-#pragma unroll
-    for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] = 0.0f;
-#pragma unroll
-    for (int r = 0; r < NG; ++r) ob[g][r] = 0.0f;
-  }
+  constexpr int WSTRIDE = G * D + 2 * G;
+  float* mw = reinterpret_cast<float*>(sm + L.ring);  // per-warp partials, once every stage is consumed
+  const TileWalk tw{sm + L.ring, full, empty, own, u0, nmine, tpb, mw};
+  constexpr bool kMma = BITS == 0 && sizeof(E) == 2;
 
   if (warp == kConsumerWarps) {
+    auto issue = [&](int i) {
+      const int s = i % F::kStages;
+      const int u = u0 + i, li = u / tpb, tile = u % tpb, j = own[li];
+      const int row = bh * p.cap_local + (j / P) * S + tile * TS;
+      uint8_t* st = sm + L.ring + s * F::kStageBytes;
+      mbar_arrive_expect_tx(full + s, 2 * F::kKvTileBytes + 4 * F::kSbTileBytes);
+#pragma unroll
+      for (int bx = 0; bx < F::kNBox; ++bx) {
+        tma_load_2d(st + bx * TS * F::kBoxBytes, &tmK, bx * F::kBoxBytes, row, full + s);
+        tma_load_2d(st + F::kKvTileBytes + bx * TS * F::kBoxBytes, &tmV, bx * F::kBoxBytes, row, full + s);
+      }
+      if constexpr (BITS != 0) {
+        const size_t so = size_t(row) * NG * sizeof(E);
+        uint8_t* sb = st + 2 * F::kKvTileBytes;
+        bulk_load(sb, static_cast<const uint8_t*>(p.k_scales) + so, F::kSbTileBytes, full + s);
+        bulk_load(sb + F::kSbTileBytes, static_cast<const uint8_t*>(p.k_biases) + so, F::kSbTileBytes, full + s);
+        bulk_load(sb + 2 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_scales) + so, F::kSbTileBytes,
+                  full + s);
+        bulk_load(sb + 3 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_biases) + so, F::kSbTileBytes,
+                  full + s);
+      }
+    };
     if (lane == 0) {
       fence_proxy_async_shared();
       fence_proxy_async_global();
-      for (int i = 0; i < nmine; ++i) {
+      for (int i = 0; i < min(nmine, F::kStages); ++i) issue(i);
+    }
+    __syncwarp();
+    // The completed block's summary before any wait for a free stage.
+    if (completing) finish_summary();
+    if (lane == 0) {
+      for (int i = F::kStages; i < nmine; ++i) {
         const int s = i % F::kStages;
-        if (i >= F::kStages && !mbar_wait(empty + s, uint32_t((i / F::kStages) - 1) & 1u, p.err)) break;
-        const int u = u0 + i, li = u / tpb, tile = u % tpb, j = own[li];
-        const int row = bh * p.cap_local + (j / P) * S + tile * TS;
-        uint8_t* st = sm + L.ring + s * F::kStageBytes;
-        mbar_arrive_expect_tx(full + s, 2 * F::kKvTileBytes + 4 * F::kSbTileBytes);
-#pragma unroll
-        for (int bx = 0; bx < F::kNBox; ++bx) {
-          tma_load_2d(st + bx * TS * F::kBoxBytes, &tmK, bx * F::kBoxBytes, row, full + s);
-          tma_load_2d(st + F::kKvTileBytes + bx * TS * F::kBoxBytes, &tmV, bx * F::kBoxBytes, row, full + s);
-        }
-        if constexpr (BITS != 0) {
-          const size_t so = size_t(row) * NG * sizeof(E);
-          uint8_t* sb = st + 2 * F::kKvTileBytes;
-          bulk_load(sb, static_cast<const uint8_t*>(p.k_scales) + so, F::kSbTileBytes, full + s);
-          bulk_load(sb + F::kSbTileBytes, static_cast<const uint8_t*>(p.k_biases) + so, F::kSbTileBytes, full + s);
-          bulk_load(sb + 2 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_scales) + so, F::kSbTileBytes,
-                    full + s);
-          bulk_load(sb + 3 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_biases) + so, F::kSbTileBytes,
-                    full + s);
-        }
+        if (!mbar_wait(empty + s, uint32_t((i / F::kStages) - 1) & 1u, p.err)) break;
+        issue(i);
       }
     }
     __syncwarp();
-    // A block that just filled up gets its summary key now (it stops being the
-    // recent block at the next step). The producer warp is otherwise idle.
-    if (appending && (T % S) == 0) {
-      const size_t row0 = size_t(bh) * p.cap_local + size_t((NB - 1) / P) * S;
-      E* dst = static_cast<E*>(p.summ) + (size_t(bh) * p.nb_stride + (NB - 1) / P) * D;
-      block_summary<E, BITS, D>(p.k_data, p.k_scales, p.k_biases, row0, S, dst, lane, 32);
-    }
+  } else if constexpr (kMma) {
+    consume_tiles_mma<E, D, G>(p, tw, qg, warp, lane);
   } else {
     float* ps = reinterpret_cast<float*>(sm + L.ps + warp * align_up(TS * G * NG * 4, 16));
-    const uint32_t ps_a = smem_u32(ps);
-    const uint32_t qf_a = smem_u32(qf);
-    for (int i = warp; i < nmine; i += kConsumerWarps) {
-      const int s = i % F::kStages;
-      const bool ok = mbar_wait(full + s, uint32_t(i / F::kStages) & 1u, p.err);
-      if (ok) {
-        const int u = u0 + i, li = u / tpb, tile = u % tpb, j = own[li];
-        const int nv = min(TS, T - (j * S + tile * TS));
-        const uint32_t kb = smem_u32(sm + L.ring + s * F::kStageBytes);
-        const uint32_t vb = kb + F::kKvTileBytes;
-        const uint32_t sbb = kb + 2 * F::kKvTileBytes;
-        // --- QK: lane = token row ---
-        const int t = lane;
-        float sc[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) sc[g] = 0.0f;
-        float acc[G][NG];
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-          for (int r = 0; r < NG; ++r) acc[g][r] = 0.0f;
-#pragma unroll
-        for (int ch = 0; ch < F::kNChunk; ++ch) {
-          const int bx = ch / F::kCpb, cc = ch % F::kCpb;
-          const uint4 raw = lds128(kb + bx * TS * F::kBoxBytes + swz(uint32_t(t * F::kBoxBytes + cc * 16), F::kCpb));
-          const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-          for (int wi = 0; wi < 4; ++wi) {
-            constexpr int EPW = F::kEpc / 4;  // elements per 32-bit word
-            float f[EPW];
-            if constexpr (BITS == 8) {
-#pragma unroll
-              for (int e = 0; e < EPW; ++e) f[e] = code_u8(wv[wi], e);
-            } else if constexpr (BITS == 4) {
-#pragma unroll
-              for (int e = 0; e < EPW; ++e) f[e] = code_u4(wv[wi], e);
-            } else {
-              unpack_word<E>(wv[wi], f);
-            }
-#pragma unroll
-            for (int e = 0; e < EPW; ++e) {
-              const int d = ch * F::kEpc + wi * EPW + e;
-              float qv[G];
-              if constexpr (G % 4 == 0) {
-#pragma unroll
-                for (int g4 = 0; g4 < G; g4 += 4) {
-                  const float4 x = lds_f4(qf_a + (d * G + g4) * 4);
-                  qv[g4] = x.x; qv[g4 + 1] = x.y; qv[g4 + 2] = x.z; qv[g4 + 3] = x.w;
-                }
-              } else {
-#pragma unroll
-                for (int g = 0; g < G; ++g) qv[g] = qf[d * G + g];
-              }
-              if constexpr (BITS == 0) {
-#pragma unroll
-                for (int g = 0; g < G; ++g) sc[g] = fmaf(qv[g], f[e], sc[g]);
-              } else {
-                const int grp = d / 64;
-#pragma unroll
-                for (int g = 0; g < G; ++g) acc[g][grp] = fmaf(qv[g], f[e], acc[g][grp]);
-              }
-            }
-          }
-        }
-        float vsc[NG], vbi[NG];
-        if constexpr (BITS != 0) {
-          const E* ksc = reinterpret_cast<const E*>(sm + (sbb - smem_u32(sm)));
-          const E* kbi = ksc + TS * NG;
-          const E* vs = ksc + 2 * TS * NG;
-          const E* vbp = ksc + 3 * TS * NG;
-#pragma unroll
-          for (int r = 0; r < NG; ++r) {
-            const float s_ = Elt<E>::to_f32(ksc[t * NG + r]);
-            const float b_ = Elt<E>::to_f32(kbi[t * NG + r]);
-#pragma unroll
-            for (int g = 0; g < G; ++g) sc[g] = fmaf(s_, acc[g][r], fmaf(b_, qs[g * NG + r], sc[g]));
-            vsc[r] = Elt<E>::to_f32(vs[t * NG + r]);
-            vbi[r] = Elt<E>::to_f32(vbp[t * NG + r]);
-          }
-        }
-        // --- online softmax over the tile (log2 domain) ---
-        const bool valid = t < nv;
-        float pv[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float s_ = valid ? sc[g] : -INFINITY;
-          const float mx = warp_max(s_);
-          const float mn = fmaxf(m_run[g], mx);
-          const float alpha = exp2f(m_run[g] - mn);
-          pv[g] = valid ? exp2f(s_ - mn) : 0.0f;
-          l_run[g] = l_run[g] * alpha + warp_sum(pv[g]);
-#pragma unroll
-          for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] *= alpha;
-          m_run[g] = mn;
-          if constexpr (BITS != 0) {
-#pragma unroll
-            for (int r = 0; r < NG; ++r) ob[g][r] = ob[g][r] * alpha + warp_sum(valid ? pv[g] * vbi[r] : 0.0f);
-          }
-        }
-        if constexpr (BITS == 0) {
-#pragma unroll
-          for (int g = 0; g < G; ++g) ps[t * G + g] = pv[g];
-        } else {
-#pragma unroll
-          for (int r = 0; r < NG; ++r)
-#pragma unroll
-            for (int g = 0; g < G; ++g) ps[(t * NG + r) * G + g] = pv[g] * vsc[r];
-        }
-        __syncwarp();
-        // --- PV: lane owns kPiece bytes (kDpl dims) of rows rr, rr+kRpp, ... ---
-        const int rr = lane / F::kLpr, pi = lane % F::kLpr;
-        const int byte0 = pi * F::kPiece;
-        const int chunk = byte0 / 16, within = byte0 % 16;
-        const int bx = chunk / F::kCpb, cc = chunk % F::kCpb;
-        const int grp = (pi * F::kDpl) / 64;
-        for (int r = rr; r < nv; r += F::kRpp) {
-          float pg[G];
-          const uint32_t pa = ps_a + ((BITS == 0 ? r : r * NG + grp) * G) * 4;
-          if constexpr (G % 4 == 0) {
-#pragma unroll
-            for (int g4 = 0; g4 < G; g4 += 4) {
-              const float4 x = lds_f4(pa + g4 * 4);
-              pg[g4] = x.x; pg[g4 + 1] = x.y; pg[g4 + 2] = x.z; pg[g4 + 3] = x.w;
-            }
-          } else {
-#pragma unroll
-            for (int g = 0; g < G; ++g) pg[g] = ps[(BITS == 0 ? r : r * NG + grp) * G + g];
-          }
-          const uint32_t va = vb + bx * TS * F::kBoxBytes + swz(uint32_t(r * F::kBoxBytes + cc * 16), F::kCpb) + within;
-          float v[F::kDpl];
-          if constexpr (F::kPiece == 16) {
-            const uint4 x = lds128(va);
-            unpack_word<E>(x.x, v);
-            unpack_word<E>(x.y, v + F::kDpl / 4);
-            unpack_word<E>(x.z, v + F::kDpl / 2);
-            unpack_word<E>(x.w, v + 3 * F::kDpl / 4);
-          } else if constexpr (F::kPiece == 8) {
-            const uint2 x = lds64(va);
-            unpack_word<E>(x.x, v);
-            unpack_word<E>(x.y, v + F::kDpl / 2);
-          } else {
-            const uint32_t x = lds32(va);
-            if constexpr (BITS == 8) {
-#pragma unroll
-              for (int e = 0; e < F::kDpl; ++e) v[e] = code_u8(x, e);
-            } else if constexpr (BITS == 4) {
-#pragma unroll
-              for (int e = 0; e < F::kDpl; ++e) v[e] = code_u4(x, e);
-            } else {
-              unpack_word<E>(x, v);
-            }
-          }
-#pragma unroll
-          for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] = fmaf(pg[g], v[e], o_acc[g][e]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty + s);
-    }
-    // Fold the row groups of the PV mapping together.
-#pragma unroll
-    for (int o = F::kLpr; o < 32; o <<= 1)
-#pragma unroll
-      for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] += __shfl_xor_sync(0xffffffffu, o_acc[g][e], o);
-    if constexpr (BITS != 0) {
-      const int grp = ((lane % F::kLpr) * F::kDpl) / 64;
-#pragma unroll
-      for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] += ob[g][grp];
-    }
+    consume_tiles_fma<E, BITS, D, G>(p, tw, qf, qs, ps, warp, lane);
   }
-  __syncthreads();  // every stage consumed: the ring is free for the merge
+  __syncthreads();  // warp partials are in mw
 
   // ---------------- phase 4: merge ----------------
-  constexpr int WSTRIDE = G * D + 2 * G;
-  float* mw = reinterpret_cast<float*>(sm + L.ring);
-  if (warp < kConsumerWarps) {
-    float* w = mw + warp * WSTRIDE;
-    if (lane == 0) {
-#pragma unroll
-      for (int g = 0; g < G; ++g) { w[g] = m_run[g]; w[G + g] = l_run[g]; }
-    }
-    if (lane < F::kLpr) {
-      const int d0 = lane * F::kDpl;
-#pragma unroll
-      for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int e = 0; e < F::kDpl; ++e) w[2 * G + g * D + d0 + e] = o_acc[g][e];
-    }
-  }
-  __syncthreads();
   float* cpart = reinterpret_cast<float*>(sm + L.cpart);  // [G] m, [G] l, [G][D] o
   for (int idx = tid; idx < G * D; idx += kThreads) {
     const int g = idx / D, d = idx % D;
@@ -532,21 +792,37 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     if (d == 0) { cpart[g] = M; cpart[G + g] = Ls; }
     cpart[2 * G + g * D + d] = O;
   }
-  if (C > 1) cluster_sync(); else __syncthreads();
-
-  const int tot = G * D;
-  const int e0 = int((long long)crank * tot / C), e1 = int((long long)(crank + 1) * tot / C);
-  const uint32_t cp_a = smem_u32(cpart);
+  // Push this CTA's partial to the CTA that owns each output element (and
+  // (m, l) to everyone), one cluster barrier, then merge from local memory.
+  constexpr int GD = G * D;
+  const int RS = 2 * G + (GD + C - 1) / C;  // per-source stride of the receive buffer
+  float* recv = reinterpret_cast<float*>(sm + L.recv);
+  auto e_lo = [&](int r) { return r * GD / C; };
+  __syncthreads();
+  if (C > 1) {
+    const uint32_t ra = smem_u32(recv) + uint32_t(crank * RS) * 4u;
+    for (int idx = tid; idx < GD; idx += kThreads) {
+      const int owner = (idx * C + C - 1) / GD;
+      st_cluster_u32(map_rank(ra + uint32_t(2 * G + idx - e_lo(owner)) * 4u, uint32_t(owner)),
+                     __float_as_uint(cpart[2 * G + idx]));
+    }
+    for (int idx = tid; idx < C * 2 * G; idx += kThreads) {
+      const int r = idx / (2 * G), k = idx % (2 * G);
+      st_cluster_u32(map_rank(ra + uint32_t(k) * 4u, uint32_t(r)), __float_as_uint(cpart[k]));
+    }
+    cluster_sync();
+  }
+  const int e0 = e_lo(crank), e1 = e_lo(crank + 1);
   for (int idx = e0 + tid; idx < e1; idx += kThreads) {
     const int g = idx / D, d = idx % D;
     float M = -INFINITY;
-    for (int r = 0; r < C; ++r) M = fmaxf(M, C > 1 ? ld_cluster_f32(map_rank(cp_a + g * 4, r)) : cpart[g]);
+    for (int r = 0; r < C; ++r) M = fmaxf(M, C > 1 ? recv[r * RS + g] : cpart[g]);
     float Ls = 0.0f, O = 0.0f;
     if (M != -INFINITY) {
       for (int r = 0; r < C; ++r) {
-        const float mr = C > 1 ? ld_cluster_f32(map_rank(cp_a + g * 4, r)) : cpart[g];
-        const float lr = C > 1 ? ld_cluster_f32(map_rank(cp_a + (G + g) * 4, r)) : cpart[G + g];
-        const float orr = C > 1 ? ld_cluster_f32(map_rank(cp_a + (2 * G + g * D + d) * 4, r)) : cpart[2 * G + g * D + d];
+        const float mr = C > 1 ? recv[r * RS + g] : cpart[g];
+        const float lr = C > 1 ? recv[r * RS + G + g] : cpart[G + g];
+        const float orr = C > 1 ? recv[r * RS + 2 * G + idx - e0] : cpart[2 * G + idx];
         const float f = exp2f(mr - M);
         Ls += lr * f;
         O += orr * f;
@@ -560,7 +836,6 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       if (d == 0) { p.part_ml[bq * 2] = M; p.part_ml[bq * 2 + 1] = Ls; }
     }
   }
-  if (C > 1) cluster_sync();
 }
 
 // LSE merge of P shard partials (rank order) into the output [B, Hq, D].

@@ -167,6 +167,11 @@ __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Fetch a tensor map (kernel parameter) into the descriptor cache early.
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 // 2-D tiled TMA load of one box into this CTA's shared memory (no multicast).
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
                                             uint64_t* bar) {
@@ -183,6 +188,56 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
           smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Warp-level tensor-core pieces (m16n8k16, fp32 accumulation)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+// c += A(16x16, row-major) * B(16x8, col-major); the A registers of rows
+// 8..15 are passed as zero (at most 8 query heads per group).
+template <typename E>
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float* c, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void mma16816<__half>(float* c, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+// Two floats -> packed 16-bit pair (x in the low half), round to nearest even.
+template <typename E> __device__ __forceinline__ uint32_t pack2(float x, float y);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float x, float y) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float x, float y) {
+  __half2 h = __floats2half2_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// (x, y) = hi + lo with hi, lo packed 16-bit pairs: ~16 significant bits.
+template <typename E> __device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t& lo) {
+  hi = pack2<E>(x, y);
+  float hx[2];
+  unpack_word<E>(hi, hx);
+  lo = pack2<E>(x - hx[0], y - hx[1]);
+}
+__device__ __forceinline__ void named_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -210,7 +265,7 @@ __device__ __forceinline__ void st_cluster_v2(uint32_t addr, uint32_t a, uint32_
 }
 __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
   return v;
 }
 
@@ -226,6 +281,31 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// Sort 32 keys held one per lane into descending lane order (bitonic network
+// over shuffles; no shared memory, no barriers).
+__device__ __forceinline__ unsigned long long warp_sort_desc(unsigned long long x, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const unsigned long long y = __shfl_xor_sync(0xffffffffu, x, j);
+      const bool up = (lane & k) == 0, lower = (lane & j) == 0;
+      x = (lower == up) ? (x > y ? x : y) : (x < y ? x : y);
+    }
+  }
+  return x;
+}
+
+// Number of entries of a descending list of distinct keys that exceed x.
+__device__ __forceinline__ int count_greater(const unsigned long long* a, int len, unsigned long long x) {
+  int lo = 0, hi = len;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (a[mid] > x) lo = mid + 1; else hi = mid;
+  }
+  return lo;
 }
 
 // Exclusive scan of one int per thread over the whole CTA (all threads call).

@@ -9,7 +9,7 @@ namespace sd {
 constexpr int kTileTokens = 32;                 // tokens per staged tile (one per lane in QK)
 constexpr int kConsumerWarps = 8;               // warps that attend
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + one TMA producer warp
-constexpr int kRingBytes = 128 * 1024;          // TMA ring; aliases the selection buffers
+constexpr int kRingBytes = 160 * 1024;          // TMA ring; aliases the selection buffers
 constexpr int kLocalKeysMax = 16384;            // candidate blocks scored by one CTA
 constexpr int kUnionMax = 8192;                 // candidates gathered for the final top-K
 constexpr int kMaxTopK = 1023;                  // K (recent block excluded)
@@ -57,9 +57,10 @@ struct Layout {
   int sel;         // (kMaxTopK + 2) ints: selected blocks, ascending, recent last
   int own;         // (kMaxTopK + 2) ints: the selected blocks stored on this shard
   int hist;        // 256 u32
-  int scratch;     // 64 ints: scans, radix state, counters
+  int scratch;     // 128 ints: scans [0,33), radix state [40,48), selection tables [64,112)
   int ps;          // per consumer warp: kTileTokens * G * groups floats
   int cpart;       // G*(D+2) floats: this CTA's merged (m, l, o)
+  int recv;        // partials pushed by the cluster for this CTA's output slice
   int bars;        // 2 * 16 mbarriers
   int total;
 };
@@ -75,9 +76,10 @@ __host__ __device__ inline Layout make_layout(int D, int G, int groups) {
   L.sel = off; off += align_up((kMaxTopK + 2) * 4, 16);
   L.own = off; off += align_up((kMaxTopK + 2) * 4, 16);
   L.hist = off; off += 256 * 4;
-  L.scratch = off; off += 64 * 4;
+  L.scratch = off; off += 128 * 4;
   L.ps = off; off += kConsumerWarps * align_up(kTileTokens * G * groups * 4, 16);
   L.cpart = off; off += align_up(G * (D + 2) * 4, 16);
+  L.recv = off; off += align_up((G * D + 16 + 2 * G * 16) * 4, 16);
   L.bars = off; off += 32 * 8;
   L.total = off;
   return L;

@@ -66,14 +66,16 @@ __device__ __forceinline__ void quantize_row_warp(const E* src, uint32_t* wq, E*
 template <typename E, int BITS, int D>
 __device__ __forceinline__ float load_key_elt(const void* data, const void* scales, const void* biases,
                                               size_t row, int d) {
+  // L2-only loads (ld.global.cg): rows may have been written by another CTA
+  // of the cluster earlier in the same launch.
   if constexpr (BITS == 0) {
-    return Elt<E>::to_f32(static_cast<const E*>(data)[row * D + d]);
+    return Elt<E>::to_f32(__ldcg(static_cast<const E*>(data) + row * D + d));
   } else {
     constexpr int PER_WORD = 32 / BITS, WORDS = D / PER_WORD, NG = D / 64;
-    const uint32_t w = static_cast<const uint32_t*>(data)[row * WORDS + d / PER_WORD];
+    const uint32_t w = __ldcg(static_cast<const uint32_t*>(data) + row * WORDS + d / PER_WORD);
     const float code = float((w >> (BITS * (d % PER_WORD))) & ((1u << BITS) - 1u));
-    const float s = Elt<E>::to_f32(static_cast<const E*>(scales)[row * NG + d / 64]);
-    const float b = Elt<E>::to_f32(static_cast<const E*>(biases)[row * NG + d / 64]);
+    const float s = Elt<E>::to_f32(__ldcg(static_cast<const E*>(scales) + row * NG + d / 64));
+    const float b = Elt<E>::to_f32(__ldcg(static_cast<const E*>(biases) + row * NG + d / 64));
     return __fmaf_rn(s, code, b);
   }
 }
@@ -90,6 +92,27 @@ __device__ __forceinline__ void block_summary(const void* data, const void* scal
     for (int i = 1; i < n; ++i) acc = __fadd_rn(acc, load_key_elt<E, BITS, D>(data, scales, biases, row0 + i, d));
     dst[d] = Elt<E>::from_f32(__fdiv_rn(acc, float(n)));
   }
+}
+
+// Sum of column d over n >= 1 rows starting at `row0` in the canonical order
+// (start from row 0, sequential fp32 adds). Loads are issued 64 rows at a
+// time before the adds, so a block of up to 64 rows costs one memory round
+// trip plus the add chain.
+template <typename E, int BITS, int D>
+__device__ __forceinline__ float column_sum(const void* data, const void* scales, const void* biases, size_t row0,
+                                            int n, int d) {
+  constexpr int BATCH = 64;
+  float acc = 0.0f;
+  for (int i0 = 0; i0 < n; i0 += BATCH) {
+    float v[BATCH];
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i)
+      v[i] = (i0 + i < n) ? load_key_elt<E, BITS, D>(data, scales, biases, row0 + i0 + i, d) : 0.0f;
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i)
+      if (i0 + i < n) acc = (i0 + i == 0) ? v[i] : __fadd_rn(acc, v[i]);
+  }
+  return acc;
 }
 
 // Write one token row of K and V (warp 0: K, warp 1: V) at local row `row`.
