@@ -124,6 +124,7 @@ def build_layers(w, n_layers: int, rank: int, world: int, seed0: int = 1000):
         idx = SparseIndex(w.B, w.Hq, w.Hkv, w.D, w.S, w.K, w.T, w.dtype, w.bits, shard_rank=rank, shard_count=world)
         k, v = case["k"], case["v"]
         idx.append(k[:, :, : w.T - 1].contiguous(), v[:, :, : w.T - 1].contiguous())
+        idx.set_launch_overlap(True)
         layers.append({"idx": idx, "q": case["q"].contiguous(), "k_new": k[:, :, w.T - 1].contiguous(),
                        "v_new": v[:, :, w.T - 1].contiguous(), "out": torch.empty_like(case["q"])})
         del case, k, v

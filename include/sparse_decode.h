@@ -84,9 +84,10 @@ typedef struct {
   int64_t cap_local;   /* token rows per (b, kv-head) on this shard */
   int64_t nb_local;    /* block rows per (b, kv-head) on this shard */
   int32_t row_bytes;   /* bytes of one K (or V) row */
-  int32_t cluster_size;
-  int32_t smem_bytes;  /* dynamic shared memory of the decode kernel */
-  int32_t reserved[5];
+  int32_t cluster_size; /* CTAs per cluster in decode */
+  int32_t smem_bytes;   /* dynamic shared memory of the decode kernel */
+  int32_t replicas;     /* clusters per (batch, kv-head) in decode */
+  int32_t reserved[4];
 } sd_arrays;
 
 int32_t sd_abi_version(void);
@@ -149,6 +150,17 @@ int32_t sd_shard_attend(sd_index* idx, const void* q, const float* all_cand_scor
                         float scale, float* part_ml, float* part_o, int32_t* sel_out, sd_stream stream);
 int32_t sd_shard_merge(sd_index* idx, const float* all_part_ml, const float* all_part_o, void* out,
                        sd_stream stream);
+
+/* Decode launches of this index may overlap the previous kernel on the
+ * stream (programmatic dependent launch): the decode kernel starts its
+ * prologue -- barrier setup and the first loads of this index's summary keys
+ * -- while the previous kernel finishes, and waits for it before reading the
+ * queries or the new token. The library remembers which index it last
+ * launched work for on each stream and never reads an index early after its
+ * own work; with overlap enabled, the caller must not write this index's
+ * arrays (sd_index_arrays) with its own kernels on the same stream. No
+ * counterpart in the reference (MLX schedules lazily evaluated graphs). */
+int32_t sd_set_launch_overlap(sd_index* idx, int32_t enable);
 
 /* Read and clear the device error word of the index (synchronises the stream).
  * *flags (host pointer) receives the bits: 1 = a bounded wait expired. */

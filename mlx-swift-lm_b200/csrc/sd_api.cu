@@ -9,7 +9,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "../../include/sparse_decode.h"
 #include "sd_format.h"
@@ -73,6 +75,26 @@ sd::KernelSet lookup(int dtype, int bits, int D, int G) {
   }
 }
 
+// Last index whose work was launched on each stream: a decode that overlaps
+// its predecessor may read its own index state early only when that
+// predecessor belongs to another index.
+std::mutex g_stream_mu;
+std::unordered_map<cudaStream_t, const void*> g_stream_last;
+
+bool note_stream(cudaStream_t st, const void* idx) {
+  std::lock_guard<std::mutex> lk(g_stream_mu);
+  auto it = g_stream_last.find(st);
+  const bool other = it == g_stream_last.end() || it->second != idx;
+  g_stream_last[st] = idx;
+  return other;
+}
+
+void forget_index(const void* idx) {
+  std::lock_guard<std::mutex> lk(g_stream_mu);
+  for (auto it = g_stream_last.begin(); it != g_stream_last.end();)
+    it = it->second == idx ? g_stream_last.erase(it) : std::next(it);
+}
+
 }  // namespace
 
 struct sd_index {
@@ -82,12 +104,19 @@ struct sd_index {
   int64_t cap_global, nb_global;
   int64_t cap_local, nb_local;
   int64_t offset;
-  int C;
+  int C, R;             // cluster size and replica clusters per (b, kv-head)
   size_t smem;
   void* arena;
   size_t arena_bytes;
   void *k_data, *v_data, *k_scales, *k_biases, *v_scales, *v_biases, *summ;
+  float* rep_part;      // R > 1: replica partials; rep_cnt: arrival counters
+  int* rep_cnt;
+  float* racc;          // 2 x [BH, D] running sums of the recent block's rows
+  int racc_cur;         // buffer holding the current sums
+  bool racc_valid;      // the current buffer matches the cache
+  bool racc_undo;       // the other buffer holds the sums before the last single-token append
   int* d_err;
+  int overlap;          // launch decodes with programmatic stream serialization
   CUtensorMap tmK, tmV;
   sd::KernelSet ks;
   bool attrs_set;
@@ -185,21 +214,33 @@ int32_t choose_cluster(sd_index* x) {
     if (!fits(c.cluster_size))
       return fail(SD_ERR_SHAPE, "cluster_size %d is too small for this capacity or top_k", c.cluster_size);
     x->C = c.cluster_size;
+    x->R = 1;
     if (max_active_clusters(x, x->C) < 1)
       return fail(SD_ERR_SHAPE, "cluster size %d cannot be scheduled with %zu bytes of shared memory", x->C, x->smem);
     return SD_OK;
   }
+  // Replicas (R <= 4 clusters per group, each attending 1/R of the tiles)
+  // raise the number of CTAs that pull from HBM: pick the largest
+  // B*Hkv*C*R <= SMs whose clusters are all resident at once, larger C first.
+  int best_c = 0, best_r = 0;
   for (int C = 16; C >= 1; --C) {
-    if (!fits(C) || BH * C > n_sm) continue;
-    if (max_active_clusters(x, C) >= BH) {
-      x->C = C;
-      return SD_OK;
+    if (!fits(C)) continue;
+    const int mac = max_active_clusters(x, C);
+    for (int R = 1; R <= 4; ++R) {
+      if (BH * C * R > n_sm || mac < BH * R) break;
+      if (C * R > best_c * best_r) { best_c = C; best_r = R; }
     }
+  }
+  if (best_c) {
+    x->C = best_c;
+    x->R = best_r;
+    return SD_OK;
   }
   // More groups than the GPU holds at once: the smallest feasible cluster.
   for (int C = 1; C <= 16; ++C)
     if (fits(C) && max_active_clusters(x, C) >= 1) {
       x->C = C;
+      x->R = 1;
       return SD_OK;
     }
   return fail(SD_ERR_SHAPE, "no schedulable cluster size for this configuration");
@@ -227,23 +268,36 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   p.out = out; p.sel_out = sel_out; p.scores_out = scores_out;
   p.cand_score = cand_score; p.cand_block = cand_block; p.part_ml = part_ml; p.part_o = part_o;
   p.err = x->d_err;
+  {
+    const int64_t BHD = int64_t(c.batch) * c.n_kv_heads * c.head_dim;
+    p.racc_in = x->racc + int64_t(x->racc_cur) * BHD;
+    p.racc_out = x->racc + int64_t(1 - x->racc_cur) * BHD;
+    p.racc_rebuild = x->racc_valid ? 0 : 1;
+  }
+  p.R = x->R;
+  p.rep_part = x->rep_part;
+  p.rep_cnt = x->rep_cnt;
+  const bool other_before = note_stream(st, x);
+  p.pdl_early = (x->overlap && other_before) ? 1 : 0;
   const int64_t ncand = p.NB - 1;
   const int64_t nloc = ncand > p.pr ? (ncand - p.pr + p.P - 1) / p.P : 0;
   if ((nloc + x->C - 1) / x->C > sd::kLocalKeysMax)
     return fail(SD_ERR_SHAPE, "too many blocks per CTA (%lld) for cluster size %d", (long long)((nloc + x->C - 1) / x->C), x->C);
 
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(unsigned(x->C), unsigned(c.batch * c.n_kv_heads), 1);
+  cfg.gridDim = dim3(unsigned(x->C * x->R), unsigned(c.batch * c.n_kv_heads), 1);
   cfg.blockDim = dim3(sd::kThreads, 1, 1);
   cfg.dynamicSmemBytes = x->smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = unsigned(x->C);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = x->overlap ? 2 : 1;
   void* args[3] = {&p, &x->tmK, &x->tmV};
   SD_CUDA(cudaLaunchKernelExC(&cfg, x->ks.decode, args));
   return SD_OK;
@@ -259,9 +313,25 @@ int32_t launch_summaries(sd_index* x, int64_t jl0, int64_t jl1, int64_t T, cudaS
   sp.jl0 = int(jl0);
   sp.k_data = x->k_data; sp.k_scales = x->k_scales; sp.k_biases = x->k_biases; sp.summ = x->summ;
   void* args[1] = {&sp};
+  note_stream(st, x);
   SD_CUDA(cudaLaunchKernel(x->ks.summary, dim3(unsigned(jl1 - jl0), unsigned(c.batch * c.n_kv_heads)), dim3(128),
                            args, 0, st));
   return SD_OK;
+}
+
+// A single-token append went through a decode launch: the running sums
+// moved to the other buffer; the old one still holds the sums before it.
+void appended_one(sd_index* x) {
+  // only the shard that stores the recent block keeps its sums
+  const int64_t j = (x->offset - 1) / x->cfg.block_size;
+  if ((j % x->cfg.shard_count) == x->cfg.shard_rank) {
+    x->racc_cur = 1 - x->racc_cur;
+    x->racc_valid = true;
+    x->racc_undo = true;
+  } else {
+    x->racc_valid = false;
+    x->racc_undo = false;
+  }
 }
 
 // Local blocks [jl0, jl1) of this shard whose global index falls in [jg0, jg1].
@@ -334,7 +404,11 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
   const size_t kv = align256(size_t(BH) * x->cap_local * x->row_bytes);
   const size_t sb = c.kv_bits ? align256(size_t(BH) * x->cap_local * x->groups * x->esize) : 0;
   const size_t su = align256(size_t(BH) * x->nb_local * c.head_dim * x->esize);
-  x->arena_bytes = 2 * kv + 4 * sb + su + 256;
+  const int GD = x->G * c.head_dim;
+  const size_t rp = x->R > 1 ? align256(size_t(BH) * x->R * x->C * (2 * x->G + (GD + x->C - 1) / x->C) * 4) : 0;
+  const size_t rcn = x->R > 1 ? align256(size_t(BH) * x->C * 4) : 0;
+  const size_t ra = align256(size_t(2) * BH * c.head_dim * 4);
+  x->arena_bytes = 2 * kv + 4 * sb + su + rp + rcn + ra + 256;
   cudaError_t e = cudaMalloc(&x->arena, x->arena_bytes);
   if (e != cudaSuccess) {
     delete x;
@@ -350,6 +424,9 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
     x->v_biases = a; a += sb;
   }
   x->summ = a; a += su;
+  x->rep_part = rp ? reinterpret_cast<float*>(a) : nullptr; a += rp;
+  x->rep_cnt = rcn ? reinterpret_cast<int*>(a) : nullptr; a += rcn;
+  x->racc = reinterpret_cast<float*>(a); a += ra;
   x->d_err = reinterpret_cast<int*>(a);
   e = cudaMemset(x->arena, 0, x->arena_bytes);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -371,6 +448,7 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
 
 int32_t sd_index_destroy(sd_index* x) {
   if (!x) return SD_OK;
+  forget_index(x);
   cudaError_t e = cudaFree(x->arena);
   delete x;
   if (e != cudaSuccess) return fail(SD_ERR_CUDA, "cudaFree failed: %s", cudaGetErrorString(e));
@@ -394,6 +472,7 @@ int32_t sd_index_arrays(const sd_index* x, sd_arrays* out) {
   out->nb_local = x->nb_local;
   out->row_bytes = x->row_bytes;
   out->cluster_size = x->C;
+  out->replicas = x->R;
   out->smem_bytes = int32_t(x->smem);
   return SD_OK;
 }
@@ -412,6 +491,9 @@ int32_t sd_index_copy(const sd_index* src, sd_index** out, sd_stream stream) {
   SD_CUDA(cudaMemcpyAsync(x->arena, src->arena, src->arena_bytes - 256, cudaMemcpyDeviceToDevice,
                           static_cast<cudaStream_t>(stream)));
   x->offset = src->offset;
+  x->racc_cur = src->racc_cur;
+  x->racc_valid = src->racc_valid;
+  x->racc_undo = src->racc_undo;
   return SD_OK;
 }
 
@@ -433,6 +515,7 @@ int32_t sd_append(sd_index* x, const void* keys, const void* values, int32_t n, 
   ap.k_data = x->k_data; ap.v_data = x->v_data;
   ap.k_scales = x->k_scales; ap.k_biases = x->k_biases; ap.v_scales = x->v_scales; ap.v_biases = x->v_biases;
   void* args[1] = {&ap};
+  note_stream(st, x);
   SD_CUDA(cudaLaunchKernel(x->ks.append, dim3(unsigned((n + 3) / 4), unsigned(c.batch * c.n_kv_heads)), dim3(256),
                            args, 0, st));
   const int64_t T = x->offset + n;
@@ -441,6 +524,8 @@ int32_t sd_append(sd_index* x, const void* keys, const void* values, int32_t n, 
   int32_t rc = launch_summaries(x, jl0, jl1, T, st);
   if (rc != SD_OK) return rc;
   x->offset = T;
+  x->racc_valid = false;
+  x->racc_undo = false;
   return SD_OK;
 }
 
@@ -448,6 +533,13 @@ int32_t sd_trim(sd_index* x, int32_t n, int32_t* trimmed) {
   if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
   if (n < 0) return fail(SD_ERR_INVALID_ARG, "n must be >= 0");
   const int64_t t = std::min<int64_t>(x->offset, n);
+  if (t == 1 && x->racc_undo) {
+    x->racc_cur = 1 - x->racc_cur;  // the sums before the last appended row
+    x->racc_valid = true;
+  } else if (t > 0) {
+    x->racc_valid = false;
+  }
+  x->racc_undo = false;
   x->offset -= t;
   if (trimmed) *trimmed = int32_t(t);
   return SD_OK;
@@ -457,6 +549,8 @@ int32_t sd_set_offset(sd_index* x, int64_t offset) {
   if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
   if (offset < 0 || offset > x->cap_global) return fail(SD_ERR_CAPACITY, "offset %lld out of range", (long long)offset);
   x->offset = offset;
+  x->racc_valid = false;
+  x->racc_undo = false;
   return SD_OK;
 }
 
@@ -479,7 +573,10 @@ int32_t sd_decode(sd_index* x, const void* q, const void* k_new, const void* v_n
   if (T < 1) return fail(SD_ERR_STATE, "decode on an empty cache");
   int32_t rc = launch_decode(x, sd::MODE_FUSED, int(T), q, k_new, v_new, scale, out, sel_out, scores_out, nullptr,
                              nullptr, nullptr, nullptr, static_cast<cudaStream_t>(stream));
-  if (rc == SD_OK) x->offset = T;
+  if (rc == SD_OK) {
+    x->offset = T;
+    if (k_new) appended_one(x);
+  }
   return rc;
 }
 
@@ -491,18 +588,12 @@ int32_t sd_shard_candidates(sd_index* x, const void* q, const void* k_new, const
   const int64_t T = x->offset + (k_new ? 1 : 0);
   if (T > x->cap_global) return fail(SD_ERR_CAPACITY, "decode append exceeds capacity %lld", (long long)x->cap_global);
   if (T < 1) return fail(SD_ERR_STATE, "decode on an empty cache");
-  if (x->cfg.top_k == 0) {
-    x->offset = T;
-    if (k_new) {
-      // Nothing to rank; still store the token on its owner shard.
-      return launch_decode(x, sd::MODE_CANDIDATES, int(T), q, k_new, v_new, scale, nullptr, nullptr, scores_out,
-                           cand_score, cand_block, nullptr, nullptr, static_cast<cudaStream_t>(stream));
-    }
-    return SD_OK;
-  }
   int32_t rc = launch_decode(x, sd::MODE_CANDIDATES, int(T), q, k_new, v_new, scale, nullptr, nullptr, scores_out,
                              cand_score, cand_block, nullptr, nullptr, static_cast<cudaStream_t>(stream));
-  if (rc == SD_OK) x->offset = T;
+  if (rc == SD_OK) {
+    x->offset = T;
+    if (k_new) appended_one(x);
+  }
   return rc;
 }
 
@@ -523,6 +614,12 @@ int32_t sd_shard_merge(sd_index* x, const float* all_ml, const float* all_o, voi
   int P = c.shard_count, BQ = c.batch * c.n_q_heads, D = c.head_dim;
   void* args[6] = {&P, &BQ, &D, const_cast<float**>(&all_ml), const_cast<float**>(&all_o), &out};
   SD_CUDA(cudaLaunchKernel(x->ks.merge, dim3(unsigned(BQ)), dim3(128), args, 0, static_cast<cudaStream_t>(stream)));
+  return SD_OK;
+}
+
+int32_t sd_set_launch_overlap(sd_index* x, int32_t enable) {
+  if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
+  x->overlap = enable ? 1 : 0;
   return SD_OK;
 }
 

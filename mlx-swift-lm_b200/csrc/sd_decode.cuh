@@ -25,6 +25,10 @@
 //   phase 4  merge: warp partials -> CTA partial -> every CTA pushes its
 //            partial to the CTA owning each output slice (DSMEM), one cluster
 //            barrier, log-sum-exp merge from local shared memory.
+// With R > 1 replica clusters per group, every replica scores and selects
+// (cheap, identical results) and attends 1/R of the tiles; the replicas'
+// partials meet in a small global buffer where the last one to arrive at
+// each output slice merges them (no waiting on other clusters).
 // Sharded decode (MODE_CANDIDATES / MODE_ATTEND) runs phases 0-2 and 2-4 as
 // two launches around the caller's all-gather of candidates.
 // Stage-4 semantics follow quantizedScaledDotProductAttention
@@ -399,8 +403,10 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   const Layout L = make_layout(D, G, NG);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int C = p.C;
+  const int C = p.C, R = p.R;
   const int crank = C > 1 ? int(cluster_ctarank()) : 0;
+  const int rep = blockIdx.x / C;  // replica cluster of this CTA
+  const int Q = C * R, qrank = rep * C + crank;
   const int bh = blockIdx.y, b = bh / p.Hkv, h = bh % p.Hkv;
   const int K = p.K, P = p.P, pr = p.pr, S = p.S, T = p.T, NB = p.NB;
 
@@ -422,6 +428,12 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   uint2* pick = reinterpret_cast<uint2*>(sm + L.ring);
 
   // ---------------- phase 0: barriers, queries, append ----------------
+  // With a programmatic launch, the next kernel may start its own prologue
+  // now; everything that the previous kernel may have produced (queries, the
+  // new token, and this index unless pdl_early says otherwise) is read only
+  // after griddep_wait.
+  if (tid == 0) griddep_launch_dependents();
+  if (!p.pdl_early) griddep_wait();
   if (tid == 0) {
     for (int s = 0; s < F::kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     fence_mbar_init();
@@ -432,9 +444,8 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   }
   const bool owner_recent = ((NB - 1) % P) == pr;
   const bool appending = p.k_new != nullptr && p.mode != MODE_ATTEND && owner_recent && crank == C - 1;
-  // The appended token fills its block: the block's summary is computed in
-  // this launch (after the barrier that publishes the appended row), split by
-  // columns over the cluster's CTAs.
+  // The appended token fills its block: its summary key is written in this
+  // launch (from the running column sums).
   const bool completing = p.k_new != nullptr && p.mode != MODE_ATTEND && owner_recent && (T % S) == 0;
 
   const int ncand = NB - 1;  // candidate blocks [0, NB-1); the recent block is always taken
@@ -461,6 +472,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     }
   }
 
+  if (p.pdl_early) griddep_wait();
   const E* qg = static_cast<const E*>(p.q) + (size_t(b) * p.Hq + size_t(h) * G) * D;
   for (int i = tid; i < G * D; i += kThreads) {
     const int g = i / D, d = i % D;
@@ -471,6 +483,25 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
 #pragma unroll
     for (int g = 1; g < G; ++g) a = __fadd_rn(a, Elt<E>::to_f32(qg[g * D + tid]));
     qsum[tid] = a;
+  }
+  // Running column sums of the recent block (fp32, rows in order -- the
+  // canonical summary order): acc = acc_before + appended row; when the
+  // appended row fills the block, its summary key is acc / S. One CTA per
+  // group (the appender of replica 0) keeps them.
+  if (appending && rep == 0 && tid < D) {
+    const int d = tid, pos = (T - 1) % S;
+    const size_t row0 = size_t(bh) * p.cap_local + size_t((NB - 1) / P) * S;
+    const float v = appended_value<E, BITS, D>(static_cast<const E*>(p.k_new) + size_t(bh) * D, d);
+    float acc = v;
+    if (pos > 0) {
+      const float before = p.racc_rebuild ? column_sum<E, BITS, D>(p.k_data, p.k_scales, p.k_biases, row0, pos, d)
+                                          : p.racc_in[size_t(bh) * D + d];
+      acc = __fadd_rn(before, v);
+    }
+    p.racc_out[size_t(bh) * D + d] = acc;
+    if (completing)
+      static_cast<E*>(p.summ)[(size_t(bh) * p.nb_stride + (NB - 1) / P) * D + d] =
+          Elt<E>::from_f32(__fdiv_rn(acc, float(S)));
   }
   if (appending && warp < 2) {
     const int t = T - 1;
@@ -599,39 +630,72 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       }
     }
     __syncthreads();
+    // Every CTA ranks only its own list against the others (pulled through
+    // DSMEM after one barrier) and publishes how many of its entries made the
+    // group's top-K (a prefix of its list) with a second barrier.
+    int* rank_own = reinterpret_cast<int*>(flag);  // kr ints (flag area is free here)
+    for (int i = tid; i < kr; i += kThreads) rank_own[i] = i;
     if (C > 1) {
-      const uint32_t la = smem_u32(mine);
-      for (int pidx = tid; pidx < kr * C; pidx += kThreads) {
-        const int r = pidx / kr, i = pidx - r * kr;
-        if (r == crank) continue;
-        const unsigned long long x = mine[i];
-        st_cluster_v2(map_rank(la + i * 8, uint32_t(r)), uint32_t(x), uint32_t(x >> 32));
-      }
       cluster_sync();
+      // one flat pass over the union: every remote load in flight before any store
+      const uint32_t la = smem_u32(lists);
+      for (int ub = tid; ub < U; ub += kThreads * 4) {
+        uint32_t lo[4], hi[4];
+        int dst[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int u = ub + k * kThreads;
+          dst[k] = -1;
+          if (u < U) {
+            int r = 0;
+            while (r + 1 < C && u >= lbase[r + 1]) ++r;
+            if (r != crank) {
+              dst[k] = r * KS + (u - lbase[r]);
+              const uint32_t ra = map_rank(la + uint32_t(dst[k]) * 8u, uint32_t(r));
+              asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];" : "=r"(lo[k]), "=r"(hi[k]) : "r"(ra));
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (dst[k] >= 0) lists[dst[k]] = (uint64_t(hi[k]) << 32) | lo[k];
+      }
+      __syncthreads();
+      for (int item = tid; item < kr * C; item += kThreads) {
+        const int i = item / C, r2 = item - i * C;
+        if (r2 == crank) continue;
+        const int c = count_greater(lists + r2 * KS, llen[r2], mine[i]);
+        if (c) atomicAdd(&rank_own[i], c);
+      }
     }
-    for (int u = tid; u < U; u += kThreads) {
-      int r = 0;
-      while (r + 1 < C && u >= lbase[r + 1]) ++r;
-      const int i = u - lbase[r];
-      const unsigned long long x = lists[r * KS + i];
-      int rank = i;
-      for (int r2 = 0; r2 < C; ++r2)
-        if (r2 != r) rank += count_greater(lists + r2 * KS, llen[r2], x);
-      const bool selected = rank < K;
-      flag[u] = selected ? 1 : 0;
-      if (selected) atomicAdd(&cnt[r], 1);
+    __syncthreads();
+    // selected entries of this CTA's list: the prefix with rank < K
+    for (int i = tid; i < kr; i += kThreads) {
+      const bool in = rank_own[i] < K;
+      const bool next_in = i + 1 < kr && rank_own[i + 1] < K;
+      if (in && !next_in) scratch[115] = i + 1;
+    }
+    if (tid == 0 && (kr == 0 || rank_own[0] >= K)) scratch[115] = 0;
+    __syncthreads();
+    if (C > 1) {
+      const int c_own = scratch[115];
+      if (tid < C) st_cluster_u32(map_rank(smem_u32(&cnt[crank]), uint32_t(tid)), uint32_t(c_own));
+      cluster_sync();
+    } else {
+      if (tid == 0) cnt[0] = scratch[115];
     }
     __syncthreads();
     kk = min(K, U);
-    for (int u = tid; u < U; u += kThreads) {
-      if (!flag[u]) continue;
-      int r = 0, before = 0;
-      while (r + 1 < C && u >= lbase[r + 1]) { before += cnt[r]; ++r; }
-      const unsigned long long x = lists[r * KS + (u - lbase[r])];
-      const uint32_t jx = 0xffffffffu - uint32_t(x);
-      int pos = before;
-      for (int i2 = 0; i2 < cnt[r]; ++i2) pos += (0xffffffffu - uint32_t(lists[r * KS + i2])) < jx ? 1 : 0;
-      pick[pos] = make_uint2(uint32_t(x >> 32), jx);
+    // the selection in list order (rank by rank, key order inside a list);
+    // the ascending order that sel_out reports is produced off the critical
+    // path by the producer warp
+    for (int item = tid; item < C * KS; item += kThreads) {
+      const int r = item / KS, i = item - r * KS;
+      if (i >= cnt[r]) continue;
+      int before = 0;
+      for (int r2 = 0; r2 < r; ++r2) before += cnt[r2];
+      const unsigned long long x = lists[r * KS + i];
+      pick[before + i] = make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x));
     }
     __syncthreads();
   } else {
@@ -659,26 +723,8 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     }
   }
 
-  // The completed block's summary (its last row is the appended one,
-  // published by the barrier above), columns split over the cluster; run by
-  // the producer warp.
-  constexpr int SCOLS = (D + 31) / 32;
-  auto finish_summary = [&]() {
-    const int sc0 = crank * D / C, sc1 = (crank + 1) * D / C;
-    const size_t crow0 = size_t(bh) * p.cap_local + size_t((NB - 1) / P) * S;
-    E* dst = static_cast<E*>(p.summ) + (size_t(bh) * p.nb_stride + (NB - 1) / P) * D;
-#pragma unroll
-    for (int k = 0; k < SCOLS; ++k) {
-      const int d = sc0 + lane + 32 * k;
-      if (d < sc1)
-        dst[d] = Elt<E>::from_f32(
-            __fdiv_rn(column_sum<E, BITS, D>(p.k_data, p.k_scales, p.k_biases, crow0, S, d), float(S)));
-    }
-  };
-
   if (p.mode == MODE_CANDIDATES) {
-    if (completing && warp == kConsumerWarps) finish_summary();
-    if (crank == 0) {
+    if (crank == 0 && rep == 0) {
       for (int i = tid; i < K; i += kThreads) {
         const bool v = i < kk;
         p.cand_score[size_t(bh) * K + i] = v ? key_score(pick[i].x) : -INFINITY;
@@ -688,22 +734,11 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     return;
   }
 
-  // Selected blocks ascending, then the recent block.
-  if (p.mode == MODE_FUSED) {
-    for (int i = tid; i < kk; i += kThreads) sel[i] = int(pick[i].y);
-  } else {
-    for (int i = tid; i < kk; i += kThreads) {
-      const int ji = int(pick[i].y);
-      int pos = 0;
-      for (int m = 0; m < kk; ++m) pos += int(pick[m].y) < ji ? 1 : 0;
-      sel[pos] = ji;
-    }
-  }
+  // Selected blocks (in selection order), then the recent block.
+  for (int i = tid; i < kk; i += kThreads) sel[i] = int(pick[i].y);
   if (tid == 0) sel[kk] = NB - 1;
   __syncthreads();
   const int n_sel = kk + 1;
-  if (p.sel_out && crank == 0)
-    for (int i = tid; i <= K; i += kThreads) p.sel_out[size_t(bh) * (K + 1) + i] = i < n_sel ? sel[i] : -1;
 
   // Blocks of this shard (all of them when P == 1), order kept.
   int* own = reinterpret_cast<int*>(sm + L.own);
@@ -721,7 +756,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   const int tpb = S / TS;
   const int recent_tiles = (T - (NB - 1) * S + TS - 1) / TS;
   const int n_units = owner_recent ? (nown - 1) * tpb + recent_tiles : nown * tpb;
-  const int u0 = crank * n_units / C, u1 = (crank + 1) * n_units / C;
+  const int u0 = qrank * n_units / Q, u1 = (qrank + 1) * n_units / Q;
   const int nmine = u1 - u0;
   constexpr int WSTRIDE = G * D + 2 * G;
   float* mw = reinterpret_cast<float*>(sm + L.ring);  // per-warp partials, once every stage is consumed
@@ -757,8 +792,17 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       for (int i = 0; i < min(nmine, F::kStages); ++i) issue(i);
     }
     __syncwarp();
-    // The completed block's summary before any wait for a free stage.
-    if (completing) finish_summary();
+    // sel_out: the selected blocks ascending (rank counting), recent last, -1 padded
+    if (p.sel_out && crank == 0 && rep == 0) {
+      int32_t* so = p.sel_out + size_t(bh) * (K + 1);
+      for (int i = lane; i < kk; i += 32) {
+        const int ji = sel[i];
+        int pos = 0;
+        for (int m = 0; m < kk; ++m) pos += sel[m] < ji ? 1 : 0;
+        so[pos] = ji;
+      }
+      for (int i = kk + lane; i <= K; i += 32) so[i] = i == kk ? NB - 1 : -1;
+    }
     if (lane == 0) {
       for (int i = F::kStages; i < nmine; ++i) {
         const int s = i % F::kStages;
@@ -813,21 +857,8 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     cluster_sync();
   }
   const int e0 = e_lo(crank), e1 = e_lo(crank + 1);
-  for (int idx = e0 + tid; idx < e1; idx += kThreads) {
+  auto emit = [&](int idx, float M, float Ls, float O) {
     const int g = idx / D, d = idx % D;
-    float M = -INFINITY;
-    for (int r = 0; r < C; ++r) M = fmaxf(M, C > 1 ? recv[r * RS + g] : cpart[g]);
-    float Ls = 0.0f, O = 0.0f;
-    if (M != -INFINITY) {
-      for (int r = 0; r < C; ++r) {
-        const float mr = C > 1 ? recv[r * RS + g] : cpart[g];
-        const float lr = C > 1 ? recv[r * RS + G + g] : cpart[G + g];
-        const float orr = C > 1 ? recv[r * RS + 2 * G + idx - e0] : cpart[2 * G + idx];
-        const float f = exp2f(mr - M);
-        Ls += lr * f;
-        O += orr * f;
-      }
-    }
     const size_t bq = size_t(b) * p.Hq + size_t(h) * G + g;
     if (p.mode == MODE_FUSED) {
       static_cast<E*>(p.out)[bq * D + d] = Elt<E>::from_f32(Ls > 0.0f ? O / Ls : 0.0f);
@@ -835,7 +866,67 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       p.part_o[bq * D + d] = O;
       if (d == 0) { p.part_ml[bq * 2] = M; p.part_ml[bq * 2 + 1] = Ls; }
     }
+  };
+  // this cluster's (M, L) per head, from the partials pushed above
+  float* hdr = reinterpret_cast<float*>(scratch);  // [2G] floats (G <= 8); the scan area is free here
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int r = 0; r < C; ++r) M = fmaxf(M, C > 1 ? recv[r * RS + tid] : cpart[tid]);
+    float Ls = 0.0f;
+    if (M != -INFINITY)
+      for (int r = 0; r < C; ++r) {
+        const float mr = C > 1 ? recv[r * RS + tid] : cpart[tid];
+        Ls += (C > 1 ? recv[r * RS + G + tid] : cpart[G + tid]) * exp2f(mr - M);
+      }
+    hdr[tid] = M;
+    hdr[G + tid] = Ls;
   }
+  __syncthreads();
+  // replica slot of this CTA's slice: [2G header][slice]
+  const int RSZ = 2 * G + (GD + C - 1) / C;
+  float* slot = R > 1 ? p.rep_part + ((size_t(bh) * R + rep) * C + crank) * RSZ : nullptr;
+  for (int idx = e0 + tid; idx < e1; idx += kThreads) {
+    const int g = idx / D;
+    const float M = hdr[g];
+    float O = 0.0f;
+    if (M != -INFINITY) {
+      for (int r = 0; r < C; ++r) {
+        const float mr = C > 1 ? recv[r * RS + g] : cpart[g];
+        const float orr = C > 1 ? recv[r * RS + 2 * G + idx - e0] : cpart[2 * G + idx];
+        O += orr * exp2f(mr - M);
+      }
+    }
+    if (R == 1) emit(idx, M, hdr[G + g], O);
+    else slot[2 * G + idx - e0] = O;
+  }
+  if (R == 1) return;
+  // Replicas: publish this slice, count arrivals; the last replica to arrive
+  // merges all R slices (in replica order) and resets the counter.
+  if (tid < 2 * G) slot[tid] = hdr[tid];
+  __threadfence();
+  __syncthreads();
+  int* last = scratch + 127;
+  if (tid == 0) *last = atomicAdd(&p.rep_cnt[bh * C + crank], 1) == R - 1 ? 1 : 0;
+  __syncthreads();
+  if (!*last) return;
+  __threadfence();
+  const float* base = p.rep_part + (size_t(bh) * R * C + crank) * RSZ;  // replica rr at + rr*C*RSZ
+  for (int idx = e0 + tid; idx < e1; idx += kThreads) {
+    const int g = idx / D;
+    float M = -INFINITY;
+    for (int rr = 0; rr < R; ++rr) M = fmaxf(M, __ldcg(base + size_t(rr) * C * RSZ + g));
+    float Ls = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+      for (int rr = 0; rr < R; ++rr) {
+        const float* sl = base + size_t(rr) * C * RSZ;
+        const float f = exp2f(__ldcg(sl + g) - M);
+        Ls += __ldcg(sl + G + g) * f;
+        O += __ldcg(sl + 2 * G + idx - e0) * f;
+      }
+    }
+    emit(idx, M, Ls, O);
+  }
+  if (tid == 0) p.rep_cnt[bh * C + crank] = 0;
 }
 
 // LSE merge of P shard partials (rank order) into the output [B, Hq, D].

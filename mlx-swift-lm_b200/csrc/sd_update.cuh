@@ -115,6 +115,35 @@ __device__ __forceinline__ float column_sum(const void* data, const void* scales
   return acc;
 }
 
+// Element d of the appended key row as the cache stores it: the row itself
+// for dense caches; for 4/8-bit caches the dequantized code, found with the
+// same fp32 steps as quantize_row_warp (group min/max are order-free).
+template <typename E, int BITS, int D>
+__device__ __forceinline__ float appended_value(const E* row, int d) {
+  if constexpr (BITS == 0) {
+    return Elt<E>::to_f32(row[d]);
+  } else {
+    const float n_bins = float((1 << BITS) - 1);
+    const int g0 = (d / 64) * 64;
+    float wmax = -INFINITY, wmin = INFINITY;
+    for (int i = 0; i < 64; ++i) {
+      const float w = Elt<E>::to_f32(row[g0 + i]);
+      wmax = fmaxf(wmax, w);
+      wmin = fminf(wmin, w);
+    }
+    float scale = fmaxf(__fdiv_rn(__fsub_rn(wmax, wmin), n_bins), 1e-7f);
+    const bool mask = fabsf(wmin) > fabsf(wmax);
+    if (!mask) scale = -scale;
+    const float edge = mask ? wmin : wmax;
+    const float q0 = rintf(__fdiv_rn(edge, scale));
+    if (q0 != 0.0f) scale = __fdiv_rn(edge, q0);
+    const float bias = (q0 == 0.0f) ? 0.0f : edge;
+    float c = rintf(__fdiv_rn(__fsub_rn(Elt<E>::to_f32(row[d]), bias), scale));
+    c = fminf(fmaxf(c, 0.0f), n_bins);
+    return __fmaf_rn(Elt<E>::to_f32(Elt<E>::from_f32(scale)), c, Elt<E>::to_f32(Elt<E>::from_f32(bias)));
+  }
+}
+
 // Write one token row of K and V (warp 0: K, warp 1: V) at local row `row`.
 template <typename E, int BITS, int D>
 __device__ __forceinline__ void write_token_row(const E* src, void* data, void* scales, void* biases,

@@ -36,7 +36,7 @@ DTYPES = {"f32": 0, "f16": 1, "bf16": 2}
 EXPORTED = ["sd_abi_version", "sd_status_string", "sd_last_error", "sd_index_create", "sd_index_destroy",
             "sd_index_config", "sd_index_arrays", "sd_index_offset", "sd_index_copy", "sd_append", "sd_trim",
             "sd_set_offset", "sd_rebuild_summaries", "sd_decode", "sd_shard_candidates", "sd_shard_attend",
-            "sd_shard_merge", "sd_check_device"]
+            "sd_shard_merge", "sd_check_device", "sd_set_launch_overlap"]
 
 
 class SDError(RuntimeError):
@@ -57,7 +57,8 @@ class SDArrays(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in (
         "k_data", "v_data", "k_scales", "k_biases", "v_scales", "v_biases", "summaries")] + [
         ("cap_local", ctypes.c_int64), ("nb_local", ctypes.c_int64), ("row_bytes", ctypes.c_int32),
-        ("cluster_size", ctypes.c_int32), ("smem_bytes", ctypes.c_int32), ("reserved", ctypes.c_int32 * 5)]
+        ("cluster_size", ctypes.c_int32), ("smem_bytes", ctypes.c_int32), ("replicas", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 4)]
 
 
 _lib: Optional[ctypes.CDLL] = None
@@ -92,6 +93,7 @@ def lib() -> ctypes.CDLL:
             "sd_shard_attend": ([vp, vp, vp, vp, f32, vp, vp, vp, vp], i32),
             "sd_shard_merge": ([vp, vp, vp, vp, vp], i32),
             "sd_check_device": ([vp, ctypes.POINTER(ctypes.c_int32), vp], i32),
+            "sd_set_launch_overlap": ([vp, i32], i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -157,6 +159,7 @@ class SparseIndex:
         arr = SDArrays()
         _check(lib().sd_index_arrays(self._h, ctypes.byref(arr)))
         self._arrays = arr
+        self.replicas = arr.replicas
 
     # -- geometry -----------------------------------------------------------
     B = property(lambda s: s.cfg.batch)
@@ -278,6 +281,11 @@ class SparseIndex:
 
     def shard_merge(self, all_part_ml, all_part_o, out, stream=None) -> None:
         _check(lib().sd_shard_merge(self._h, _ptr(all_part_ml), _ptr(all_part_o), _ptr(out), _stream(stream)))
+
+    def set_launch_overlap(self, enable: bool = True) -> None:
+        """Let decode launches overlap the previous kernel on the stream
+        (programmatic dependent launch); see sd_set_launch_overlap."""
+        _check(lib().sd_set_launch_overlap(self._h, 1 if enable else 0))
 
     def check_device(self, stream=None) -> int:
         f = ctypes.c_int32()

@@ -217,3 +217,97 @@ def test_sharded_steps_on_one_gpu(cuda, P, bits):
     assert_close(to_host(out, w.dtype).reshape(-1, D), c["out"], w.dtype)
     for s in shards:
         assert s.check_device() == 0
+
+
+@pytest.mark.parametrize("bits", [0, 8])
+def test_trim_one_then_other_token(cuda, bits):
+    """Decode the token that fills a block, trim it, decode a different token
+    in its place (the running block sums are restored by the one-step undo):
+    summaries, selection and output match the oracle for the second token."""
+    import torch
+    from sparse_decode import SparseIndex
+    w = Workload("undo", B=1, Hq=8, Hkv=2, D=128, T=64 * 12, S=64, K=4, dtype="bf16", bits=bits, needles=2)
+    c = host_case(w, seed=21)
+    idx = SparseIndex(1, w.Hq, w.Hkv, w.D, w.S, w.K, w.T, w.dtype, bits)
+    k = to_dev(c["ks"].reshape(1, w.Hkv, w.T, w.D), w.dtype)
+    v = to_dev(c["vs"].reshape(1, w.Hkv, w.T, w.D), w.dtype)
+    q = to_dev(c["qs"], w.dtype)
+    idx.append(k[:, :, : w.T - 2].contiguous(), v[:, :, : w.T - 2].contiguous())
+    idx.decode(q, k[:, :, w.T - 2].contiguous(), v[:, :, w.T - 2].contiguous(), c["scale"])  # rebuilds the sums
+    rng = np.random.default_rng(5)
+    other = rng.standard_normal((w.Hkv, w.D)).astype(np.float32)
+    for rep in range(3):
+        idx.decode(q, k[:, :, w.T - 1].contiguous(), v[:, :, w.T - 1].contiguous(), c["scale"])
+        assert idx.trim(1) == 1
+        ks2 = c["ks"].reshape(w.Hkv, w.T, w.D).copy()
+        ks2[:, w.T - 1] = oracle.to_storage(other * (rep + 1), c["dt"])
+        c2 = _recompute_k(w, c, ks2)
+        kn = to_dev(ks2[:, w.T - 1].reshape(1, w.Hkv, w.D), w.dtype)
+        sel = torch.zeros((w.Hkv, w.K + 1), dtype=torch.int32, device="cuda")
+        out = idx.decode(q, kn, v[:, :, w.T - 1].contiguous(), c["scale"], sel_out=sel)
+        assert np.array_equal(sel.cpu().numpy(), c2["sel"])
+        assert_close(to_host(out, w.dtype).reshape(-1, w.D), c2["out"], w.dtype)
+        g = to_host(idx.views()["summaries"][:, : w.NB].contiguous(), w.dtype)
+        assert np.array_equal(g, oracle.to_f32(c2["summ"], c["dt"]).reshape(g.shape))
+        assert idx.trim(1) == 1
+    assert idx.check_device() == 0
+
+
+def _recompute_k(w, c, ks):
+    """Oracle results with key storage `ks` [BH, T, D] (re-quantized when needed)."""
+    dt = c["dt"]
+    if w.bits:
+        kq = oracle.quantize(ks, dt, w.D, w.bits)
+        Kc = oracle.Cache(dt, w.D, kq[0], w.bits, kq[1], kq[2])
+    else:
+        Kc = oracle.Cache(dt, w.D, ks)
+    summ = oracle.summaries(Kc, w.T, w.S, dt)
+    sc = oracle.scores(c["qs"], dt, summ, dt, w.B, w.Hq, w.Hkv, w.D, w.NB, c["scale"])
+    sel = oracle.select(sc, w.K)
+    out = oracle.attend_f64(c["qs"], dt, Kc, c["Vc"], w.B, w.Hq, w.Hkv, w.T, w.S, sel, c["scale"])
+    return {"summ": summ, "scores": sc, "sel": sel, "out": out}
+
+
+def test_overlapped_launches_across_layers(cuda):
+    """Two layers decoded alternately with launch overlap enabled (each
+    kernel may start while the other layer's kernel finishes), and the same
+    layer twice in a row (no early reads then): every step matches the oracle."""
+    import torch
+    from sparse_decode import SparseIndex
+    w = Workload("pdl", B=1, Hq=8, Hkv=2, D=128, T=64 * 20 + 40, S=64, K=6, dtype="bf16", needles=3)
+    steps = 30
+    wf = w.with_(T=w.T + steps)
+    cases = [host_case(wf, seed=31 + l) for l in range(2)]
+    idxs, dev = [], []
+    for c in cases:
+        idx = SparseIndex(1, w.Hq, w.Hkv, w.D, w.S, w.K, wf.T, w.dtype)
+        k = to_dev(c["ks"].reshape(1, w.Hkv, wf.T, w.D), w.dtype)
+        v = to_dev(c["vs"].reshape(1, w.Hkv, wf.T, w.D), w.dtype)
+        idx.append(k[:, :, : w.T - 1].contiguous(), v[:, :, : w.T - 1].contiguous())
+        idx.set_launch_overlap(True)
+        idxs.append(idx)
+        dev.append((k, v, to_dev(c["qs"], w.dtype)))
+    outs = []
+    for s in range(steps):
+        T = w.T + s
+        step_out = {}
+        # alternating order: layer 1 runs twice in a row across steps 0/1, layer 0 across 1/2, ...
+        for l in ((0, 1) if s % 2 == 0 else (1, 0)):
+            k, v, q = dev[l]
+            sel = torch.zeros((w.Hkv, w.K + 1), dtype=torch.int32, device="cuda")
+            step_out[l] = (idxs[l].decode(q, k[:, :, T - 1].contiguous(), v[:, :, T - 1].contiguous(),
+                                          cases[l]["scale"], sel_out=sel), sel)
+        outs.append((T, step_out))
+    torch.cuda.synchronize()
+    for T, step_out in outs:
+        for l, (out, sel) in step_out.items():
+            c = cases[l]
+            dt = c["dt"]
+            summ = oracle.summaries(c["Kc"], T, w.S, dt)
+            sc = oracle.scores(c["qs"], dt, summ, dt, 1, w.Hq, w.Hkv, w.D, (T + 63) // 64, c["scale"])
+            osel = oracle.select(sc, w.K)
+            ref = oracle.attend_f64(c["qs"], dt, c["Kc"], c["Vc"], 1, w.Hq, w.Hkv, T, w.S, osel, c["scale"])
+            assert np.array_equal(sel.cpu().numpy()[:, : osel.shape[1]], osel)
+            assert_close(to_host(out, w.dtype).reshape(-1, w.D), ref, w.dtype)
+    for idx in idxs:
+        assert idx.check_device() == 0
