@@ -166,6 +166,32 @@ int32_t sd_set_launch_overlap(sd_index* idx, int32_t enable);
  * *flags (host pointer) receives the bits: 1 = a bounded wait expired. */
 int32_t sd_check_device(sd_index* idx, int32_t* flags, sd_stream stream);
 
+/* Decode for callers that cannot allocate device memory. Some hosts own all
+ * of the GPU's memory themselves -- for example a serving runtime that
+ * reserves the device's memory pool when it starts and lends slices of it to
+ * plug-ins -- so a library that calls cudaMalloc behind their back can fail
+ * or fragment that pool. This entry point allocates nothing: the caller
+ * passes its own device arrays in the layout of sd_arrays (k_data, v_data,
+ * scales/biases for 4/8-bit caches, summaries, cap_local, nb_local; e.g.
+ * arrays filled earlier through an index, or by the caller's own code), the
+ * number of tokens `offset`, queries, output and an optional sel_out, and the
+ * call decodes one token (no append) like sd_decode. device_flags (nullable,
+ * a caller-owned device int, zeroed by the caller) receives the same error
+ * bits as sd_check_device reports.
+ * The kernel's scratch (replica partials and arrival counters) lives in a
+ * fixed array of SD_NOALLOC_SCRATCH_BYTES of device memory inside the
+ * library, which every GPU that loads the library keeps until the process
+ * exits. The first call on a device looks up that array's device address.
+ * All calls on a device share the array and it keeps the last call's
+ * contents (the call clears the parts that must start at zero), so two calls
+ * that overlap on the GPU race with each other: serialise them. A
+ * configuration whose scratch cannot fit (batch * n_kv_heads beyond about
+ * 16k groups) is rejected with SD_ERR_CAPACITY. Single-shard caches only.
+ * No counterpart in the reference. */
+#define SD_NOALLOC_SCRATCH_BYTES (1u << 20)
+int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arrays, int64_t offset, const void* q, float scale,
+                          void* out, int32_t* sel_out, int32_t* device_flags, sd_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -635,3 +635,156 @@ int32_t sd_check_device(sd_index* x, int32_t* flags, sd_stream stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode without device allocation (sd_decode_noalloc).
+//
+// For callers that own every byte of device memory themselves: the keys,
+// values, scales, biases and summary keys are their arrays, and the decode
+// kernel's replica partials, arrival counters and error word live in one
+// fixed array of device memory that this file defines. Every GPU that loads
+// the library holds that array until the process exits; all calls on a GPU
+// share it and it keeps the last call's contents, so calls that overlap on
+// the GPU (two streams, or two host threads) race with each other.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratch = SD_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[256] = {};  // device address of g_noalloc_scratch, per device ordinal
+
+// Device address of the scratch array on the current device. The array's
+// name is only a host-side stand-in for the symbol; the address comes from
+// cudaGetSymbolAddress, once per device, with that device current.
+int32_t noalloc_scratch(void** out) {
+  int dev = 0;
+  SD_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 256) return fail(SD_ERR_STATE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(SD_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev, cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return SD_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arrays, int64_t offset, const void* q,
+                                     float scale, void* out, int32_t* sel_out, int32_t* device_flags,
+                                     sd_stream stream) {
+  int32_t rc = validate(cfg);
+  if (rc != SD_OK) return rc;
+  if (!arrays || !q || !out) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  const sd_config& c = *cfg;
+  if (c.shard_count != 1) return fail(SD_ERR_STATE, "sd_decode_noalloc serves single-shard caches only");
+  if (!std::isfinite(scale)) return fail(SD_ERR_INVALID_ARG, "scale must be finite");
+  if (!arrays->k_data || !arrays->v_data || !arrays->summaries)
+    return fail(SD_ERR_INVALID_ARG, "k_data, v_data and summaries are required");
+  if (c.kv_bits && (!arrays->k_scales || !arrays->k_biases || !arrays->v_scales || !arrays->v_biases))
+    return fail(SD_ERR_INVALID_ARG, "quantized caches need scales and biases");
+  if (arrays->cap_local < 1 || arrays->cap_local % c.block_size != 0 || offset < 1 || offset > arrays->cap_local)
+    return fail(SD_ERR_SHAPE, "offset %lld / cap_local %lld do not describe a cache", (long long)offset,
+                (long long)arrays->cap_local);
+  if (arrays->nb_local < (offset + c.block_size - 1) / c.block_size)
+    return fail(SD_ERR_SHAPE, "nb_local %lld is smaller than the blocks in the cache", (long long)arrays->nb_local);
+
+  // A host-side description of the cache; no device memory is allocated.
+  sd_index x{};
+  x.cfg = c;
+  SD_CUDA(cudaGetDevice(&x.device));
+  x.G = c.n_q_heads / c.n_kv_heads;
+  x.esize = elt_size(c.dtype);
+  x.groups = c.kv_bits ? c.head_dim / 64 : 1;
+  x.row_bytes = c.kv_bits ? c.head_dim * c.kv_bits / 8 : c.head_dim * x.esize;
+  if (arrays->row_bytes != 0 && arrays->row_bytes != x.row_bytes)
+    return fail(SD_ERR_SHAPE, "row_bytes %d does not match the configuration (%d)", arrays->row_bytes, x.row_bytes);
+  x.cap_local = arrays->cap_local;
+  x.nb_local = arrays->nb_local;
+  x.cap_global = x.cap_local;
+  x.offset = offset;
+  const int64_t BH = int64_t(c.batch) * c.n_kv_heads;
+  if (BH * x.cap_local >= (int64_t(1) << 31) || BH > 65535)
+    return fail(SD_ERR_SHAPE, "cache too large: batch*kv_heads*cap_local rows must stay below 2^31");
+  x.ks = lookup(c.dtype, c.kv_bits, c.head_dim, x.G);
+  if (!x.ks.decode) return fail(SD_ERR_SHAPE, "no kernel for this configuration");
+  x.smem = size_t(sd::make_layout(c.head_dim, x.G, x.groups).total) + 1024;
+  rc = setup_kernels(&x);
+  if (rc == SD_OK) rc = choose_cluster(&x);
+  if (rc != SD_OK) return rc;
+
+  // Scratch layout: [0, 256) error word, then the arrival counters, then the
+  // replica partials. Fewer replicas are used if the partials do not fit;
+  // with one replica only the counters and the error word remain.
+  const int GD = x.G * c.head_dim;
+  auto part_bytes = [&](int R) {
+    return R > 1 ? size_t(BH) * R * x.C * (2 * x.G + (GD + x.C - 1) / x.C) * 4 : size_t(0);
+  };
+  const size_t cnt_bytes = align256(size_t(BH) * x.C * 4);
+  while (x.R > 1 && 256 + cnt_bytes + part_bytes(x.R) > kNoAllocScratch) --x.R;
+  if (256 + cnt_bytes + part_bytes(x.R) > kNoAllocScratch)
+    return fail(SD_ERR_CAPACITY, "batch*kv_heads (%lld) needs %zu bytes of scratch; the limit is %zu",
+                (long long)BH, 256 + cnt_bytes, kNoAllocScratch);
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc != SD_OK) return rc;
+  uint8_t* sb = static_cast<uint8_t*>(scratch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the error word and the arrival counters must start at zero
+  SD_CUDA(cudaMemsetAsync(sb, 0, 256 + cnt_bytes, st));
+
+  x.k_data = arrays->k_data; x.v_data = arrays->v_data;
+  x.k_scales = arrays->k_scales; x.k_biases = arrays->k_biases;
+  x.v_scales = arrays->v_scales; x.v_biases = arrays->v_biases;
+  x.summ = arrays->summaries;
+  rc = encode_map(&x.tmK, x.k_data, x.row_bytes, BH * x.cap_local);
+  if (rc == SD_OK) rc = encode_map(&x.tmV, x.v_data, x.row_bytes, BH * x.cap_local);
+  if (rc != SD_OK) return rc;
+
+  sd::DecodeParams p{};
+  p.B = c.batch; p.Hq = c.n_q_heads; p.Hkv = c.n_kv_heads; p.S = c.block_size; p.K = c.top_k;
+  p.T = int(offset);
+  p.NB = int((offset + c.block_size - 1) / c.block_size);
+  p.P = 1; p.pr = 0;
+  p.cap_local = int(x.cap_local);
+  p.nb_stride = int(x.nb_local);
+  p.C = x.C;
+  p.mode = sd::MODE_FUSED;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.q = q;
+  p.k_data = x.k_data; p.v_data = x.v_data;
+  p.k_scales = x.k_scales; p.k_biases = x.k_biases; p.v_scales = x.v_scales; p.v_biases = x.v_biases;
+  p.summ = x.summ;
+  p.out = out;
+  p.sel_out = sel_out;
+  p.err = device_flags ? device_flags : reinterpret_cast<int*>(sb);
+  p.R = x.R;
+  p.rep_cnt = reinterpret_cast<int*>(sb + 256);
+  p.rep_part = x.R > 1 ? reinterpret_cast<float*>(sb + 256 + cnt_bytes) : nullptr;
+  const int64_t nloc = p.NB - 1;
+  if ((nloc + x.C - 1) / x.C > sd::kLocalKeysMax)
+    return fail(SD_ERR_SHAPE, "too many blocks per CTA for cluster size %d", x.C);
+
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(unsigned(x.C * x.R), unsigned(BH), 1);
+  lc.blockDim = dim3(sd::kThreads, 1, 1);
+  lc.dynamicSmemBytes = x.smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(x.C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  void* args[3] = {&p, &x.tmK, &x.tmV};
+  SD_CUDA(cudaLaunchKernelExC(&lc, x.ks.decode, args));
+  return SD_OK;
+}

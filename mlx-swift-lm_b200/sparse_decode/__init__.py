@@ -36,7 +36,7 @@ DTYPES = {"f32": 0, "f16": 1, "bf16": 2}
 EXPORTED = ["sd_abi_version", "sd_status_string", "sd_last_error", "sd_index_create", "sd_index_destroy",
             "sd_index_config", "sd_index_arrays", "sd_index_offset", "sd_index_copy", "sd_append", "sd_trim",
             "sd_set_offset", "sd_rebuild_summaries", "sd_decode", "sd_shard_candidates", "sd_shard_attend",
-            "sd_shard_merge", "sd_check_device", "sd_set_launch_overlap"]
+            "sd_shard_merge", "sd_check_device", "sd_set_launch_overlap", "sd_decode_noalloc"]
 
 
 class SDError(RuntimeError):
@@ -94,6 +94,8 @@ def lib() -> ctypes.CDLL:
             "sd_shard_merge": ([vp, vp, vp, vp, vp], i32),
             "sd_check_device": ([vp, ctypes.POINTER(ctypes.c_int32), vp], i32),
             "sd_set_launch_overlap": ([vp, i32], i32),
+            "sd_decode_noalloc": ([ctypes.POINTER(SDConfig), ctypes.POINTER(SDArrays), i64, vp, f32, vp, vp, vp, vp],
+                                  i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
