@@ -370,9 +370,11 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
   int32_t rc = validate(cfg);
   if (rc != SD_OK) return rc;
   const sd_config& c = *cfg;
+  int device = 0;
+  SD_CUDA(cudaGetDevice(&device));
   sd_index* x = new sd_index();
   x->cfg = c;
-  SD_CUDA(cudaGetDevice(&x->device));
+  x->device = device;
   x->G = c.n_q_heads / c.n_kv_heads;
   x->esize = elt_size(c.dtype);
   x->groups = c.kv_bits ? c.head_dim / 64 : 1;
@@ -695,6 +697,10 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   if (arrays->nb_local < (offset + c.block_size - 1) / c.block_size)
     return fail(SD_ERR_SHAPE, "nb_local %lld is smaller than the blocks in the cache", (long long)arrays->nb_local);
 
+  const int row_bytes = c.kv_bits ? c.head_dim * c.kv_bits / 8 : c.head_dim * elt_size(c.dtype);
+  if (arrays->row_bytes != 0 && arrays->row_bytes != row_bytes)
+    return fail(SD_ERR_SHAPE, "row_bytes %d does not match the configuration (%d)", arrays->row_bytes, row_bytes);
+
   // A host-side description of the cache; no device memory is allocated.
   sd_index x{};
   x.cfg = c;
@@ -702,9 +708,7 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   x.G = c.n_q_heads / c.n_kv_heads;
   x.esize = elt_size(c.dtype);
   x.groups = c.kv_bits ? c.head_dim / 64 : 1;
-  x.row_bytes = c.kv_bits ? c.head_dim * c.kv_bits / 8 : c.head_dim * x.esize;
-  if (arrays->row_bytes != 0 && arrays->row_bytes != x.row_bytes)
-    return fail(SD_ERR_SHAPE, "row_bytes %d does not match the configuration (%d)", arrays->row_bytes, x.row_bytes);
+  x.row_bytes = row_bytes;
   x.cap_local = arrays->cap_local;
   x.nb_local = arrays->nb_local;
   x.cap_global = x.cap_local;

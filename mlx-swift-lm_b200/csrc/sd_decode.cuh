@@ -455,6 +455,11 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   const int c0 = chunk_lo(crank), c1 = chunk_lo(crank + 1);
   const int n = c1 - c0;
   auto jglob = [&](int i) { return (c0 + i) * P + pr; };
+  // Up to kAllKeysMax candidates: every CTA gathers all keys of the group and
+  // selects by a block-wide bitonic top-K (no second exchange).
+  const bool whole = p.mode != MODE_ATTEND && nloc <= kAllKeysMax && K <= 256;
+  uint32_t* allk = reinterpret_cast<uint32_t*>(sm + L.allk);
+  if (whole) keys = allk + c0;
 
   // Score-phase loads go out before the query barrier so that the two memory
   // latencies overlap. Warps 0..7 score; the producer warp does not.
@@ -566,7 +571,44 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
 
   // ---------------- phase 2: selection ----------------
   int kk;  // blocks chosen by top-K
-  if (p.mode != MODE_ATTEND) {
+  if (whole) {
+    if (C > 1) {
+      cluster_sync();
+      const uint32_t ab = smem_u32(allk);
+      for (int ib = tid; ib < nloc; ib += kThreads * 4) {
+        uint32_t val[4];
+        int at[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int i = ib + k * kThreads;
+          at[k] = -1;
+          if (i < nloc && (i < c0 || i >= c1)) {
+            at[k] = i;
+            val[k] = ld_cluster_u32(map_rank(ab + uint32_t(i) * 4u, uint32_t(((i + 1) * C - 1) / nloc)));
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (at[k] >= 0) allk[at[k]] = val[k];
+      }
+      __syncthreads();
+    }
+    kk = min(K, nloc);
+    auto akey = [&](int i) -> unsigned long long { return full_key(allk[i], i * P + pr); };
+    if (nloc <= K || K == 0) {
+      for (int i = tid; i < kk; i += kThreads) pick[i] = make_uint2(allk[i], uint32_t(i * P + pr));
+    } else {
+      unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 32 * 1024);
+      if (K <= 64) block_topk<2>(akey, nloc, runs, lane, warp, kThreads / 32);
+      else if (K <= 128) block_topk<4>(akey, nloc, runs, lane, warp, kThreads / 32);
+      else block_topk<8>(akey, nloc, runs, lane, warp, kThreads / 32);
+      for (int i = tid; i < kk; i += kThreads) {
+        const unsigned long long x = runs[i];
+        pick[i] = make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x));
+      }
+    }
+    __syncthreads();
+  } else if (p.mode != MODE_ATTEND) {
     // (1) This CTA's candidates (its top-K by radix select first when it holds
     // more than kRunMax) are sorted in runs of 32 in registers and ranked
     // against each other by binary search: this CTA's top-K, descending.
@@ -731,6 +773,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
         p.cand_block[size_t(bh) * K + i] = v ? int32_t(pick[i].y) : -1;
       }
     }
+    if (whole && C > 1) cluster_sync();  // peers may still be reading this CTA's keys
     return;
   }
 

@@ -265,6 +265,11 @@ __device__ __forceinline__ uint32_t map_rank(uint32_t local_smem_addr, uint32_t 
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
   return r;
 }
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
@@ -304,6 +309,109 @@ __device__ __forceinline__ unsigned long long warp_sort_desc(unsigned long long 
     }
   }
   return x;
+}
+
+// Bitonic network over L = 32*RR keys held by one warp (register r of lane l
+// holds element r*32 + l): sorts descending.
+template <int RR>
+__device__ __forceinline__ void warp_bitonic_sort_desc(unsigned long long (&v)[RR], int lane) {
+  constexpr int L = 32 * RR;
+#pragma unroll
+  for (int k = 2; k <= L; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 32) {
+        const int jr = j >> 5;
+#pragma unroll
+        for (int r = 0; r < RR; ++r) {
+          if ((r & jr) == 0) {
+            const int rp = r | jr;
+            const bool desc = ((r * 32 + lane) & k) == 0;
+            const unsigned long long x = v[r], y = v[rp];
+            const unsigned long long hi = x > y ? x : y, lo = x > y ? y : x;
+            v[r] = desc ? hi : lo;
+            v[rp] = desc ? lo : hi;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < RR; ++r) {
+          const unsigned long long y = __shfl_xor_sync(0xffffffffu, v[r], j);
+          const bool desc = ((r * 32 + lane) & k) == 0, lower = (lane & j) == 0;
+          v[r] = (lower == desc) ? (v[r] > y ? v[r] : y) : (v[r] < y ? v[r] : y);
+        }
+      }
+    }
+  }
+}
+
+// The last stage of the network: sorts a bitonic sequence descending.
+template <int RR>
+__device__ __forceinline__ void warp_bitonic_merge_desc(unsigned long long (&v)[RR], int lane) {
+  constexpr int L = 32 * RR;
+#pragma unroll
+  for (int j = L >> 1; j > 0; j >>= 1) {
+    if (j >= 32) {
+      const int jr = j >> 5;
+#pragma unroll
+      for (int r = 0; r < RR; ++r) {
+        if ((r & jr) == 0) {
+          const int rp = r | jr;
+          const unsigned long long x = v[r], y = v[rp];
+          v[r] = x > y ? x : y;
+          v[rp] = x > y ? y : x;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < RR; ++r) {
+        const unsigned long long y = __shfl_xor_sync(0xffffffffu, v[r], j);
+        v[r] = ((lane & j) == 0) ? (v[r] > y ? v[r] : y) : (v[r] < y ? v[r] : y);
+      }
+    }
+  }
+}
+
+// Top L = 32*RR of n distinct keys keyf(i) (key 0 never occurs): runs of L
+// keys are sorted by the warps, then merged pairwise -- max of run A and the
+// reversed run B is bitonic and holds the top L of both, and one bitonic
+// merge sorts it -- until runs[0 .. min(L, n)) holds the top keys,
+// descending. All CTA threads call. runs: ceil(n / L) * L u64 of shared memory.
+template <int RR, class KeyF>
+__device__ __forceinline__ void block_topk(KeyF keyf, int n, unsigned long long* runs, int lane, int warp,
+                                           int nwarps) {
+  constexpr int L = 32 * RR;
+  const int nrun = (n + L - 1) / L;
+  for (int run = warp; run < nrun; run += nwarps) {
+    unsigned long long v[RR];
+#pragma unroll
+    for (int r = 0; r < RR; ++r) {
+      const int i = run * L + r * 32 + lane;
+      v[r] = i < n ? keyf(i) : 0ull;
+    }
+    warp_bitonic_sort_desc<RR>(v, lane);
+#pragma unroll
+    for (int r = 0; r < RR; ++r) runs[run * L + r * 32 + lane] = v[r];
+  }
+  __syncthreads();
+  for (int s = 1; s < nrun; s <<= 1) {
+    for (int a = warp * 2 * s; a < nrun; a += nwarps * 2 * s) {
+      const int b = a + s;
+      if (b < nrun) {
+        unsigned long long v[RR];
+#pragma unroll
+        for (int r = 0; r < RR; ++r) {
+          const int e = r * 32 + lane;
+          const unsigned long long x = runs[a * L + e], y = runs[b * L + (L - 1 - e)];
+          v[r] = x > y ? x : y;
+        }
+        warp_bitonic_merge_desc<RR>(v, lane);
+#pragma unroll
+        for (int r = 0; r < RR; ++r) runs[a * L + r * 32 + lane] = v[r];
+      }
+    }
+    __syncthreads();
+  }
 }
 
 // Number of entries of a descending list of distinct keys that exceed x.

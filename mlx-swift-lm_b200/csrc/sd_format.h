@@ -13,6 +13,7 @@ constexpr int kRingBytes = 160 * 1024;          // TMA ring; aliases the selecti
 constexpr int kLocalKeysMax = 16384;            // candidate blocks scored by one CTA
 constexpr int kUnionMax = 8192;                 // candidates gathered for the final top-K
 constexpr int kMaxTopK = 1023;                  // K (recent block excluded)
+constexpr int kAllKeysMax = 2048;               // candidates held whole by every CTA (bitonic top-K)
 
 enum Mode { MODE_FUSED = 0, MODE_CANDIDATES = 1, MODE_ATTEND = 2 };
 
@@ -61,6 +62,7 @@ struct Layout {
   int ps;          // per consumer warp: kTileTokens * G * groups floats
   int cpart;       // G*(D+2) floats: this CTA's merged (m, l, o)
   int recv;        // partials pushed by the cluster for this CTA's output slice
+  int allk;        // kAllKeysMax u32: every candidate key of the group (bitonic top-K)
   int bars;        // 2 * 16 mbarriers
   int total;
 };
@@ -80,6 +82,7 @@ __host__ __device__ inline Layout make_layout(int D, int G, int groups) {
   L.ps = off; off += kConsumerWarps * align_up(kTileTokens * G * groups * 4, 16);
   L.cpart = off; off += align_up(G * (D + 2) * 4, 16);
   L.recv = off; off += align_up((G * D + 16 + 2 * G * 16) * 4, 16);
+  L.allk = off; off += kAllKeysMax * 4;
   L.bars = off; off += 32 * 8;
   L.total = off;
   return L;

@@ -295,30 +295,35 @@ class SparseIndex:
         return f.value
 
 
-def sharded_decode(index: SparseIndex, q, k_new=None, v_new=None, scale=None, group=None, sel_out=None):
+def sharded_decode(index, q, k_new=None, v_new=None, scale=None, group=None, sel_out=None):
     """Sequence-sharded decode step over torch.distributed (NCCL over NVLink):
     local candidates -> all-gather -> global top-K + local attention ->
     all-gather of (m, l, o) partials -> log-sum-exp merge. Every rank calls it
-    with the same q / k_new / v_new; returns out [B, Hq, D] on every rank."""
+    with the same q / k_new / v_new; returns out [B, Hq, D] on every rank.
+
+    `index` is a SparseIndex (or anything with its shard_* methods and P, B,
+    Hq, Hkv, D, K attributes). The gathers use flat views, the form that every
+    torch.distributed backend accepts."""
     import torch
     import torch.distributed as dist
     P, BH, K = index.P, index.B * index.Hkv, index.K
     BQ, D = index.B * index.Hq, index.D
     dev = q.device
-    cs = torch.empty((BH, max(K, 1)), device=dev, dtype=torch.float32)
-    cb = torch.empty((BH, max(K, 1)), device=dev, dtype=torch.int32)
+    KK = max(K, 1)
+    cs = torch.empty((BH, KK), device=dev, dtype=torch.float32)
+    cb = torch.empty((BH, KK), device=dev, dtype=torch.int32)
     index.shard_candidates(q, cs, cb, k_new, v_new, scale)
-    all_cs = torch.empty((P, BH, max(K, 1)), device=dev, dtype=torch.float32)
-    all_cb = torch.empty((P, BH, max(K, 1)), device=dev, dtype=torch.int32)
-    dist.all_gather_into_tensor(all_cs, cs, group=group)
-    dist.all_gather_into_tensor(all_cb, cb, group=group)
+    all_cs = torch.empty((P, BH, KK), device=dev, dtype=torch.float32)
+    all_cb = torch.empty((P, BH, KK), device=dev, dtype=torch.int32)
+    dist.all_gather_into_tensor(all_cs.view(-1), cs.view(-1), group=group)
+    dist.all_gather_into_tensor(all_cb.view(-1), cb.view(-1), group=group)
     ml = torch.empty((BQ, 2), device=dev, dtype=torch.float32)
     po = torch.empty((BQ, D), device=dev, dtype=torch.float32)
     index.shard_attend(q, all_cs, all_cb, ml, po, scale, sel_out)
     all_ml = torch.empty((P, BQ, 2), device=dev, dtype=torch.float32)
     all_po = torch.empty((P, BQ, D), device=dev, dtype=torch.float32)
-    dist.all_gather_into_tensor(all_ml, ml, group=group)
-    dist.all_gather_into_tensor(all_po, po, group=group)
+    dist.all_gather_into_tensor(all_ml.view(-1), ml.view(-1), group=group)
+    dist.all_gather_into_tensor(all_po.view(-1), po.view(-1), group=group)
     out = torch.empty_like(q)
     index.shard_merge(all_ml, all_po, out)
     return out
