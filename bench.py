@@ -361,7 +361,9 @@ def main() -> None:
                 "config": {"workload": w.name, "batch": w.B, "q_heads": w.Hq, "kv_heads": w.Hkv, "head_dim": w.D,
                            "context": w.T, "block": w.S, "top_k": w.K, "layers_per_step": w.layers,
                            "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
-                           "l2": "inputs larger than L2 (36 layers x 18.1 MB per step)",
+                           "l2": f"inputs larger than L2 ({w.layers} layers x {bytes_layer / 1e6:.1f} MB per step)"
+                                 if w.layers * bytes_layer > 126e6 else
+                                 f"inputs smaller than L2 ({w.layers} layers x {bytes_layer / 1e6:.1f} MB): not a bench line",
                            "cuda_graph": world == 1},
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,

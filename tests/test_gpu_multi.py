@@ -1,0 +1,102 @@
+"""Sequence-sharded decode across real GPUs (one process per GPU, NCCL): the
+output of `sparse_decode.sharded_decode` on every rank matches the oracle and
+the selection is the single-device one. Needs at least two GPUs; skipped
+otherwise."""
+from __future__ import annotations
+
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+from sparse_decode.synth import Workload
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    Workload("mg_bf16", B=2, Hq=8, Hkv=2, D=128, T=64 * 40 + 9, S=64, K=8, dtype="bf16", needles=4),
+    Workload("mg_q8", B=1, Hq=32, Hkv=8, D=128, T=128 * 20 + 1, S=128, K=5, dtype="bf16", bits=8, needles=3),
+]
+
+
+def _rank_main(rank: int, world: int, port: int, results):
+    import torch
+    import torch.distributed as dist
+    from gpu_cases import to_dev, to_host
+    from _util import host_case, rel_err
+    from sparse_decode import SparseIndex, sharded_decode
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        res = []
+        for i, w in enumerate(CASES):
+            c = host_case(w, 300 + i)
+            B, Hkv, T, D = w.B, w.Hkv, w.T, w.D
+            idx = SparseIndex(B, w.Hq, Hkv, D, w.S, w.K, T, w.dtype, w.bits, shard_rank=rank, shard_count=world)
+            k = to_dev(c["ks"].reshape(B, Hkv, T, D), w.dtype)
+            v = to_dev(c["vs"].reshape(B, Hkv, T, D), w.dtype)
+            q = to_dev(c["qs"], w.dtype)
+            idx.append(k[:, :, : T - 1].contiguous(), v[:, :, : T - 1].contiguous())
+            outs, sels = [], []
+            for rep in range(2):  # decode, trim, decode again: same result
+                sel = torch.full((B * Hkv, w.K + 1), -7, dtype=torch.int32, device="cuda")
+                out = sharded_decode(idx, q, k[:, :, T - 1].contiguous(), v[:, :, T - 1].contiguous(), c["scale"],
+                                     sel_out=sel)
+                torch.cuda.synchronize()
+                outs.append(to_host(out, w.dtype))
+                sels.append(sel.cpu().numpy()[:, : w.n_sel])
+                assert idx.trim(1) == 1
+            res.append((outs, sels, idx.check_device()))
+            idx.close()
+        results.put((rank, res))
+    except BaseException as e:  # reported to the parent, which fails the test
+        results.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2])
+def test_sharded_decode_across_gpus(cuda, world):
+    import torch
+    import torch.multiprocessing as mp
+    from _util import assert_close, host_case
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in procs:
+            rank, res = results.get(timeout=300)
+            got[rank] = res
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(world):
+        assert not isinstance(got[r], str), f"rank {r}: {got[r]}"
+    for i, w in enumerate(CASES):
+        c = host_case(w, 300 + i)
+        ref_out = None
+        for r in range(world):
+            outs, sels, err = got[r][i]
+            assert err == 0, (w.name, r)
+            for o, s in zip(outs, sels):
+                assert np.array_equal(s, c["sel"]), (w.name, r)
+                assert_close(o.reshape(-1, w.D), c["out"], w.dtype)
+                if ref_out is None:
+                    ref_out = o
+                assert np.array_equal(o, ref_out), (w.name, r)  # identical on every rank and step
