@@ -230,36 +230,36 @@ def main() -> None:
     layers = build_layers(w, w.layers, rank, world)
     stream = torch.cuda.current_stream()
     scale = 1.0 / math.sqrt(w.D)
+    # Several GPUs: the fused sequence-sharded step, one launch per layer and
+    # GPU that exchanges candidates and partials through peer memory (all
+    # layers share one exchange area).
+    comm = sparse_decode.ShardComm(layers[0]["idx"]) if world > 1 else None
+    if dist:
+        dist.barrier()
 
-    def step_device():
-        if world == 1:
-            for L in layers:
-                L["idx"].decode(L["q"], L["k_new"], L["v_new"], scale, out=L["out"])
+    def decode_layer(L, q, kn, vn, out):
+        if comm is None:
+            L["idx"].decode(q, kn, vn, scale, out=out)
         else:
-            for L in layers:
-                L["out"] = sparse_decode.sharded_decode(L["idx"], L["q"], L["k_new"], L["v_new"], scale)
-        for L in layers:
-            L["idx"].trim(1)
+            L["idx"].shard_decode(comm, q, kn, vn, scale, out=out)
 
-    # Capture the 36 single-layer launches of one step in a CUDA graph
-    # (single GPU); the launches are identical every step because the step's
-    # token is trimmed again afterwards.
-    graph = None
-    if world == 1:
-        step_device()
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            for L in layers:
-                L["idx"].decode(L["q"], L["k_new"], L["v_new"], scale, out=L["out"])
+    # Capture the 36 single-layer launches of one step in a CUDA graph; the
+    # launches are identical every step because the step's token is trimmed
+    # again afterwards.
+    for L in layers:
+        decode_layer(L, L["q"], L["k_new"], L["v_new"], L["out"])
+    for L in layers:
+        L["idx"].trim(1)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
         for L in layers:
-            L["idx"].trim(1)
+            decode_layer(L, L["q"], L["k_new"], L["v_new"], L["out"])
+    for L in layers:
+        L["idx"].trim(1)
 
     def run_step():
-        if graph is not None:
-            graph.replay()
-        else:
-            step_device()
+        graph.replay()
 
     for _ in range(args.warmup):
         run_step()
@@ -312,12 +312,8 @@ def main() -> None:
 
     def e2e_step():
         d_in.copy_(h_in, non_blocking=True)
-        if world == 1:
-            for L, (q, kn, vn), out in zip(layers, views, outs):
-                L["idx"].decode(q, kn, vn, scale, out=out)
-        else:
-            for i, (L, (q, kn, vn)) in enumerate(zip(layers, views)):
-                outs[i].copy_(sparse_decode.sharded_decode(L["idx"], q, kn, vn, scale))
+        for L, (q, kn, vn), out in zip(layers, views, outs):
+            decode_layer(L, q, kn, vn, out)
         h_out.copy_(d_out, non_blocking=True)
         for L in layers:
             L["idx"].trim(1)
@@ -360,22 +356,26 @@ def main() -> None:
                 "data": "synthetic (seeded N(0,1) Q/K/V, planted needle blocks)",
                 "config": {"workload": w.name, "batch": w.B, "q_heads": w.Hq, "kv_heads": w.Hkv, "head_dim": w.D,
                            "context": w.T, "block": w.S, "top_k": w.K, "layers_per_step": w.layers,
-                           "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+                           "parallelism": f"sequence-sharded x{world} (fused peer-memory exchange)" if world > 1
+                           else "single GPU",
                            "l2": f"inputs larger than L2 ({w.layers} layers x {bytes_layer / 1e6:.1f} MB per step)"
                                  if w.layers * bytes_layer > 126e6 else
                                  f"inputs smaller than L2 ({w.layers} layers x {bytes_layer / 1e6:.1f} MB): not a bench line",
-                           "cuda_graph": world == 1},
+                           "cuda_graph": True},
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                              "algorithmic_bytes_per_layer": bytes_layer,
                              "note": "per-layer time includes inter-launch gaps inside the CUDA graph"},
                 "e2e": {"value": round(e2e_us, 4), "unit": UNIT,
                         "h2d_bytes_per_step": n_in * esz, "d2h_bytes_per_step": n_out * esz},
-                "gpu_launches": args.steps * w.layers * (1 if world == 1 else 3),
+                "gpu_launches": args.steps * w.layers,
                 "clocks": clk.summary()}
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
+    del graph
+    if comm is not None:
+        comm.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

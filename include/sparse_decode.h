@@ -151,6 +151,42 @@ int32_t sd_shard_attend(sd_index* idx, const void* q, const float* all_cand_scor
 int32_t sd_shard_merge(sd_index* idx, const float* all_part_ml, const float* all_part_o, void* out,
                        sd_stream stream);
 
+/* Fused sequence-sharded decode over peer memory (one process per GPU, GPUs
+ * of one node with peer access, e.g. NVLink through NVSwitch). One launch
+ * per step and shard does all of the sharded path's work: local scores and
+ * top-K, the candidates' exchange, the global top-K (identical on every
+ * shard), attention over this shard's selected blocks, the exchange of the
+ * (m, l, o) partials and their log-sum-exp merge in shard order -- the
+ * exchanges are stores into the other shards' memory plus flags, so there is
+ * no collective call between kernels and the step can be captured in a CUDA
+ * graph. Every shard gets the full output.
+ *
+ * Setup, per index configuration and shard (the layers of a model that share
+ * a configuration share one sd_comm):
+ *   1. sd_comm_create(idx, &comm): the exchange area of this shard.
+ *   2. sd_comm_handle(comm, h): SD_COMM_HANDLE_BYTES of host bytes describing
+ *      it (a CUDA IPC handle plus the configuration).
+ *   3. exchange the handles between the shards by any transport (e.g. an
+ *      all-gather), in shard order, and pass all of them to sd_comm_open.
+ * Then per step, on every shard with the same arguments:
+ *   sd_shard_decode(idx, comm, q, k_new, v_new, scale, out, sel_out, stream).
+ * All shards must issue the same sequence of sd_shard_decode calls on one
+ * comm, on one stream each. The kernel waits for the other shards with a
+ * bounded wait (10 s): on expiry it sets error bit 4 (sd_check_device) and
+ * finishes. Every cluster of the launch must be resident at once: a
+ * configuration with more (b, kv-head) groups than the GPU holds is rejected
+ * with SD_ERR_SHAPE (use sd_shard_candidates / attend / merge). Destroy a
+ * comm only after every shard has finished using it (e.g. after a barrier).
+ * No counterpart in the reference. */
+typedef struct sd_comm sd_comm; /* opaque */
+#define SD_COMM_HANDLE_BYTES 128
+int32_t sd_comm_create(const sd_index* idx, sd_comm** out);
+int32_t sd_comm_handle(const sd_comm* comm, void* handle);
+int32_t sd_comm_open(sd_comm* comm, const void* handles);
+int32_t sd_comm_destroy(sd_comm* comm);
+int32_t sd_shard_decode(sd_index* idx, sd_comm* comm, const void* q, const void* k_new, const void* v_new,
+                        float scale, void* out, int32_t* sel_out, sd_stream stream);
+
 /* Decode launches of this index may overlap the previous kernel on the
  * stream (programmatic dependent launch): the decode kernel starts its
  * prologue -- barrier setup and the first loads of this index's summary keys
@@ -163,7 +199,8 @@ int32_t sd_shard_merge(sd_index* idx, const float* all_part_ml, const float* all
 int32_t sd_set_launch_overlap(sd_index* idx, int32_t enable);
 
 /* Read and clear the device error word of the index (synchronises the stream).
- * *flags (host pointer) receives the bits: 1 = a bounded wait expired. */
+ * *flags (host pointer) receives the bits: 1 = a bounded wait expired,
+ * 2 = an index out of range, 4 = a wait for another shard expired. */
 int32_t sd_check_device(sd_index* idx, int32_t* flags, sd_stream stream);
 
 /* Decode for callers that cannot allocate device memory. Some hosts own all

@@ -122,6 +122,19 @@ struct sd_index {
   bool attrs_set;
 };
 
+// Exchange area of one shard for the fused sharded step (sd_shard_decode);
+// the layout is described with DecodeParams::peer.
+struct sd_comm {
+  int device;
+  int P, pr, BH, K, C, R, G, D, RS;
+  int resident;                     // every cluster of a launch fits on the GPU at once
+  size_t bytes;
+  int64_t off_fpart, off_cand, off_part, off_ctl;
+  uint8_t* local;
+  uint8_t* peers[sd::kMaxShards];   // own area at [pr]
+  bool opened;
+};
+
 namespace {
 
 int32_t validate(const sd_config* c) {
@@ -248,7 +261,8 @@ int32_t choose_cluster(sd_index* x) {
 
 int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k_new, const void* v_new,
                       float scale, void* out, int32_t* sel_out, float* scores_out, float* cand_score,
-                      int32_t* cand_block, float* part_ml, float* part_o, cudaStream_t st) {
+                      int32_t* cand_block, float* part_ml, float* part_o, cudaStream_t st,
+                      const sd_comm* comm = nullptr) {
   const sd_config& c = x->cfg;
   sd::DecodeParams p{};
   p.B = c.batch; p.Hq = c.n_q_heads; p.Hkv = c.n_kv_heads; p.S = c.block_size; p.K = c.top_k;
@@ -278,7 +292,17 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   p.rep_part = x->rep_part;
   p.rep_cnt = x->rep_cnt;
   const bool other_before = note_stream(st, x);
-  p.pdl_early = (x->overlap && other_before) ? 1 : 0;
+  // Peer mode never overlaps launches: the exchange areas are reused by the
+  // next launch only after this one has finished everywhere.
+  const bool overlap = x->overlap && mode != sd::MODE_PEER;
+  p.pdl_early = (overlap && other_before) ? 1 : 0;
+  if (mode == sd::MODE_PEER) {
+    for (int r = 0; r < comm->P; ++r) p.peer[r] = comm->peers[r];
+    p.x_fpart = comm->off_fpart;
+    p.x_cand = comm->off_cand;
+    p.x_part = comm->off_part;
+    p.x_ctl = comm->off_ctl;
+  }
   const int64_t ncand = p.NB - 1;
   const int64_t nloc = ncand > p.pr ? (ncand - p.pr + p.P - 1) / p.P : 0;
   if ((nloc + x->C - 1) / x->C > sd::kLocalKeysMax)
@@ -297,7 +321,7 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = x->overlap ? 2 : 1;
+  cfg.numAttrs = overlap ? 2 : 1;
   void* args[3] = {&p, &x->tmK, &x->tmV};
   SD_CUDA(cudaLaunchKernelExC(&cfg, x->ks.decode, args));
   return SD_OK;
@@ -617,6 +641,136 @@ int32_t sd_shard_merge(sd_index* x, const float* all_ml, const float* all_o, voi
   void* args[6] = {&P, &BQ, &D, const_cast<float**>(&all_ml), const_cast<float**>(&all_o), &out};
   SD_CUDA(cudaLaunchKernel(x->ks.merge, dim3(unsigned(BQ)), dim3(128), args, 0, static_cast<cudaStream_t>(stream)));
   return SD_OK;
+}
+
+namespace {
+struct CommHandle {
+  cudaIpcMemHandle_t ipc;
+  int32_t magic, version, P, pr, BH, K, C, R, G, D;
+  uint64_t bytes;
+};
+static_assert(sizeof(CommHandle) <= SD_COMM_HANDLE_BYTES, "comm handle too large");
+constexpr int32_t kCommMagic = 0x53444331;  // "SDC1"
+}  // namespace
+
+int32_t sd_comm_create(const sd_index* x, sd_comm** out) {
+  if (!x || !out) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  *out = nullptr;
+  const sd_config& c = x->cfg;
+  if (c.shard_count > sd::kMaxShards)
+    return fail(SD_ERR_SHAPE, "peer exchange supports up to %d shards (got %d)", sd::kMaxShards, c.shard_count);
+  sd_comm m{};
+  m.device = x->device;
+  m.P = c.shard_count; m.pr = c.shard_rank;
+  m.BH = c.batch * c.n_kv_heads; m.K = c.top_k; m.C = x->C; m.R = x->R; m.G = x->G; m.D = c.head_dim;
+  m.RS = 2 * m.G + (m.G * m.D + m.C - 1) / m.C;
+  m.resident = max_active_clusters(x, x->C) >= int64_t(m.BH) * x->R ? 1 : 0;
+  const int64_t P = m.P, BH = m.BH;
+  m.off_fpart = int64_t(align256(size_t(P * BH * 4)));
+  m.off_cand = m.off_fpart + int64_t(align256(size_t(P * BH * m.C * 4)));
+  m.off_part = m.off_cand + int64_t(align256(size_t(P * BH * std::max(m.K, 1) * 8)));
+  m.off_ctl = m.off_part + int64_t(align256(size_t(P * BH * m.C * m.RS * 4)));
+  m.bytes = size_t(m.off_ctl) + 256;
+  int dev = 0;
+  SD_CUDA(cudaGetDevice(&dev));
+  if (dev != x->device) return fail(SD_ERR_STATE, "current device %d is not the index's device %d", dev, x->device);
+  cudaError_t e = cudaMalloc(&m.local, m.bytes);
+  if (e != cudaSuccess) return fail(SD_ERR_CUDA, "cudaMalloc(%zu) failed: %s", m.bytes, cudaGetErrorString(e));
+  e = cudaMemset(m.local, 0, m.bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(m.local);
+    return fail(SD_ERR_CUDA, "cudaMemset failed: %s", cudaGetErrorString(e));
+  }
+  m.peers[m.pr] = m.local;
+  m.opened = m.P == 1;
+  *out = new sd_comm(m);
+  return SD_OK;
+}
+
+int32_t sd_comm_handle(const sd_comm* m, void* handle) {
+  if (!m || !handle) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  CommHandle h{};
+  if (m->P > 1) SD_CUDA(cudaIpcGetMemHandle(&h.ipc, m->local));
+  h.magic = kCommMagic; h.version = 1;
+  h.P = m->P; h.pr = m->pr; h.BH = m->BH; h.K = m->K; h.C = m->C; h.R = m->R; h.G = m->G; h.D = m->D;
+  h.bytes = m->bytes;
+  std::memset(handle, 0, SD_COMM_HANDLE_BYTES);
+  std::memcpy(handle, &h, sizeof(h));
+  return SD_OK;
+}
+
+int32_t sd_comm_open(sd_comm* m, const void* handles) {
+  if (!m || !handles) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  if (m->opened) return m->P == 1 ? SD_OK : fail(SD_ERR_STATE, "comm is already open");
+  const uint8_t* hb = static_cast<const uint8_t*>(handles);
+  for (int r = 0; r < m->P; ++r) {
+    CommHandle h;
+    std::memcpy(&h, hb + size_t(r) * SD_COMM_HANDLE_BYTES, sizeof(h));
+    if (h.magic != kCommMagic || h.version != 1)
+      return fail(SD_ERR_INVALID_ARG, "handle %d is not an sd_comm handle", r);
+    if (h.pr != r || h.P != m->P)
+      return fail(SD_ERR_INVALID_ARG, "handle %d belongs to shard %d of %d (expected %d of %d)", r, h.pr, h.P, r, m->P);
+    if (h.BH != m->BH || h.K != m->K || h.C != m->C || h.R != m->R || h.G != m->G || h.D != m->D ||
+        h.bytes != m->bytes)
+      return fail(SD_ERR_SHAPE, "shard %d's index configuration (cluster %d, replicas %d) differs from this one's "
+                  "(cluster %d, replicas %d)", r, h.C, h.R, m->C, m->R);
+  }
+  for (int r = 0; r < m->P; ++r) {
+    if (r == m->pr) continue;
+    CommHandle h;
+    std::memcpy(&h, hb + size_t(r) * SD_COMM_HANDLE_BYTES, sizeof(h));
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h.ipc, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < r; ++q)
+        if (q != m->pr && m->peers[q]) { cudaIpcCloseMemHandle(m->peers[q]); m->peers[q] = nullptr; }
+      return fail(SD_ERR_CUDA, "cudaIpcOpenMemHandle(shard %d) failed: %s", r, cudaGetErrorString(e));
+    }
+    m->peers[r] = static_cast<uint8_t*>(ptr);
+  }
+  m->opened = true;
+  return SD_OK;
+}
+
+int32_t sd_comm_destroy(sd_comm* m) {
+  if (!m) return SD_OK;
+  cudaError_t e = cudaSuccess;
+  for (int r = 0; r < m->P; ++r)
+    if (r != m->pr && m->peers[r]) {
+      cudaError_t e2 = cudaIpcCloseMemHandle(m->peers[r]);
+      if (e == cudaSuccess) e = e2;
+    }
+  cudaError_t e3 = cudaFree(m->local);
+  if (e == cudaSuccess) e = e3;
+  delete m;
+  if (e != cudaSuccess) return fail(SD_ERR_CUDA, "sd_comm_destroy: %s", cudaGetErrorString(e));
+  return SD_OK;
+}
+
+int32_t sd_shard_decode(sd_index* x, sd_comm* m, const void* q, const void* k_new, const void* v_new, float scale,
+                        void* out, int32_t* sel_out, sd_stream stream) {
+  if (!x || !m || !q || !out) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  if ((k_new == nullptr) != (v_new == nullptr)) return fail(SD_ERR_INVALID_ARG, "k_new and v_new must both be given or both NULL");
+  if (!std::isfinite(scale)) return fail(SD_ERR_INVALID_ARG, "scale must be finite");
+  if (!m->opened) return fail(SD_ERR_STATE, "comm is not open (sd_comm_open)");
+  const sd_config& c = x->cfg;
+  if (m->P != c.shard_count || m->pr != c.shard_rank || m->BH != c.batch * c.n_kv_heads || m->K != c.top_k ||
+      m->C != x->C || m->R != x->R || m->G != x->G || m->D != c.head_dim || m->device != x->device)
+    return fail(SD_ERR_INVALID_ARG, "comm was created for another index configuration");
+  if (!m->resident)
+    return fail(SD_ERR_SHAPE, "%d groups x %d replica clusters do not fit on the GPU at once; use sd_shard_candidates, "
+                "sd_shard_attend and sd_shard_merge", m->BH, m->R);
+  const int64_t T = x->offset + (k_new ? 1 : 0);
+  if (T > x->cap_global) return fail(SD_ERR_CAPACITY, "decode append exceeds capacity %lld", (long long)x->cap_global);
+  if (T < 1) return fail(SD_ERR_STATE, "decode on an empty cache");
+  int32_t rc = launch_decode(x, sd::MODE_PEER, int(T), q, k_new, v_new, scale, out, sel_out, nullptr, nullptr,
+                             nullptr, nullptr, nullptr, static_cast<cudaStream_t>(stream), m);
+  if (rc == SD_OK) {
+    x->offset = T;
+    if (k_new) appended_one(x);
+  }
+  return rc;
 }
 
 int32_t sd_set_launch_overlap(sd_index* x, int32_t enable) {

@@ -409,6 +409,10 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   const int Q = C * R, qrank = rep * C + crank;
   const int bh = blockIdx.y, b = bh / p.Hkv, h = bh % p.Hkv;
   const int K = p.K, P = p.P, pr = p.pr, S = p.S, T = p.T, NB = p.NB;
+  // Peer mode: this launch's epoch. The control word changes only after every
+  // CTA of the previous launch has finished, so all CTAs read the same value.
+  const bool peer = p.mode == MODE_PEER;
+  const uint32_t epoch = peer ? *reinterpret_cast<const volatile uint32_t*>(p.peer[pr] + p.x_ctl) + 1u : 0u;
 
   float* qf = reinterpret_cast<float*>(sm + L.qf);
   float* qsum = reinterpret_cast<float*>(sm + L.qsum);
@@ -740,7 +744,23 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       pick[before + i] = make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x));
     }
     __syncthreads();
-  } else {
+  }
+  // The group's top-K of a candidate union uni[0, U) (score key, block), by
+  // radix select; every shard computes the same selection.
+  auto select_union = [&](int U) {
+    kk = min(K, U);
+    auto ukey = [&](int i) -> unsigned long long { return full_key(uni[i].x, int32_t(uni[i].y)); };
+    if (U > K && K > 0) {
+      radix_select(ukey, U, K, hist, rs);
+      const unsigned long long pre = rs->prefix, msk = rs->mask;
+      cta_compact(U, [&](int i) { return (ukey(i) & msk) >= pre; }, [&](int pos, int i) { pick[pos] = uni[i]; },
+                  scratch);
+    } else {
+      for (int i = tid; i < kk; i += kThreads) pick[i] = uni[i];
+      __syncthreads();
+    }
+  };
+  if (p.mode == MODE_ATTEND) {
     // Sharded attend: the P shards' candidates (gathered by the caller),
     // padding dropped, then the group's top-K by radix select.
     const int tot = P * K;
@@ -752,16 +772,56 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
           uni[pos] = make_uint2(score_key(p.cand_score[src(i)]), uint32_t(p.cand_block[src(i)]));
         },
         scratch);
-    kk = min(K, U);
-    auto ukey = [&](int i) -> unsigned long long { return full_key(uni[i].x, int32_t(uni[i].y)); };
-    if (U > K && K > 0) {
-      radix_select(ukey, U, K, hist, rs);
-      const unsigned long long pre = rs->prefix, msk = rs->mask;
-      cta_compact(U, [&](int i) { return (ukey(i) & msk) >= pre; }, [&](int pos, int i) { pick[pos] = uni[i]; },
-                  scratch);
-    } else {
-      for (int i = tid; i < kk; i += kThreads) pick[i] = uni[i];
+    select_union(U);
+  } else if (peer && K > 0) {
+    // Peer mode: (1) this shard's local top-K goes into every shard's
+    // exchange area (0-padded full keys) and the group's flag is released
+    // there; (2) the group waits for every shard's flag in its own area;
+    // (3) the top-K of the P*K union, identical on every shard.
+    const int BHn = int(gridDim.y);
+    if (crank == 0 && rep == 0) {
+      for (int r = 0; r < P; ++r) {
+        unsigned long long* dst =
+            reinterpret_cast<unsigned long long*>(p.peer[r] + p.x_cand) + (size_t(pr) * BHn + bh) * K;
+        for (int i = tid; i < K; i += kThreads) dst[i] = i < kk ? full_key(pick[i].x, int(pick[i].y)) : 0ull;
+      }
+      __threadfence_system();
       __syncthreads();
+      if (tid < P) {
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<uint32_t*>(p.peer[tid]) + pr * BHn + bh, epoch);
+      }
+    }
+    if (tid == 0) {
+      const uint32_t* fl = reinterpret_cast<const uint32_t*>(p.peer[pr]);
+      for (int r = 0; r < P; ++r)
+        if (!wait_epoch(fl + r * BHn + bh, epoch, p.err)) break;
+    }
+    __syncthreads();
+    const unsigned long long* ck = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_cand) + size_t(bh) * K;
+    const size_t rstride = size_t(BHn) * K;
+    auto ckey = [&](int i) -> unsigned long long { return __ldcg(ck + size_t(i / K) * rstride + (i % K)); };
+    const int N = P * K;
+    if (N <= kAllKeysMax && K <= 256) {
+      unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 32 * 1024);
+      if (K <= 64) block_topk<2>(ckey, N, runs, lane, warp, kThreads / 32);
+      else if (K <= 128) block_topk<4>(ckey, N, runs, lane, warp, kThreads / 32);
+      else block_topk<8>(ckey, N, runs, lane, warp, kThreads / 32);
+      kk = __syncthreads_count(tid < K && runs[tid] != 0ull);
+      for (int i = tid; i < kk; i += kThreads) {
+        const unsigned long long x = runs[i];
+        pick[i] = make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x));
+      }
+      __syncthreads();
+    } else {
+      const int U = cta_compact(
+          N, [&](int i) { return ckey(i) != 0ull; },
+          [&](int pos, int i) {
+            const unsigned long long x = ckey(i);
+            uni[pos] = make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x));
+          },
+          scratch);
+      select_union(U);
     }
   }
 
@@ -905,6 +965,15 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     const size_t bq = size_t(b) * p.Hq + size_t(h) * G + g;
     if (p.mode == MODE_FUSED) {
       static_cast<E*>(p.out)[bq * D + d] = Elt<E>::from_f32(Ls > 0.0f ? O / Ls : 0.0f);
+    } else if (peer) {
+      // this shard's record of (group, slice) -- [2G (m, l)][slice of o] --
+      // into every shard's exchange area
+      const size_t ro = ((size_t(pr) * gridDim.y + bh) * C + crank) * RS;
+      for (int r = 0; r < P; ++r) {
+        float* rec = reinterpret_cast<float*>(p.peer[r] + p.x_part) + ro;
+        rec[2 * G + idx - e0] = O;
+        if (idx == e0 || d == 0) { rec[g] = M; rec[G + g] = Ls; }
+      }
     } else {
       p.part_o[bq * D + d] = O;
       if (d == 0) { p.part_ml[bq * 2] = M; p.part_ml[bq * 2 + 1] = Ls; }
@@ -942,7 +1011,61 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     if (R == 1) emit(idx, M, hdr[G + g], O);
     else slot[2 * G + idx - e0] = O;
   }
-  if (R == 1) return;
+  // Peer mode: every CTA counts itself finished in its own area; the last one
+  // of the launch resets the count and publishes the epoch.
+  auto peer_finish = [&]() {
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t* ctl = reinterpret_cast<uint32_t*>(p.peer[pr] + p.x_ctl);
+      __threadfence();
+      if (atomicAdd(ctl + 1, 1u) == gridDim.x * gridDim.y - 1u) {
+        ctl[1] = 0u;
+        __threadfence();
+        ctl[0] = epoch;
+      }
+    }
+  };
+  // Peer mode, after this shard's record of the slice went out: release the
+  // slice's flag in every area, wait for every shard's record of it here, and
+  // merge them in shard order (the same output on every shard).
+  auto peer_combine = [&]() {
+    const int BHn = int(gridDim.y);
+    __threadfence_system();
+    __syncthreads();
+    if (tid < P) {
+      __threadfence_system();
+      st_release_sys(reinterpret_cast<uint32_t*>(p.peer[tid] + p.x_fpart) + (size_t(pr) * BHn + bh) * C + crank,
+                     epoch);
+    }
+    if (tid == 0) {
+      const uint32_t* fl = reinterpret_cast<const uint32_t*>(p.peer[pr] + p.x_fpart);
+      for (int r = 0; r < P; ++r)
+        if (!wait_epoch(fl + (size_t(r) * BHn + bh) * C + crank, epoch, p.err)) break;
+    }
+    __syncthreads();
+    const float* recs = reinterpret_cast<const float*>(p.peer[pr] + p.x_part);
+    auto rec = [&](int r) { return recs + ((size_t(r) * BHn + bh) * C + crank) * RS; };
+    for (int idx = e0 + tid; idx < e1; idx += kThreads) {
+      const int g = idx / D, d = idx % D;
+      float M = -INFINITY;
+      for (int r = 0; r < P; ++r) M = fmaxf(M, __ldcg(rec(r) + g));
+      float Ls = 0.0f, O = 0.0f;
+      if (M != -INFINITY) {
+        for (int r = 0; r < P; ++r) {
+          const float f = exp2f(__ldcg(rec(r) + g) - M);
+          Ls += __ldcg(rec(r) + G + g) * f;
+          O += __ldcg(rec(r) + 2 * G + idx - e0) * f;
+        }
+      }
+      const size_t bq = size_t(b) * p.Hq + size_t(h) * G + g;
+      static_cast<E*>(p.out)[bq * D + d] = Elt<E>::from_f32(Ls > 0.0f ? O / Ls : 0.0f);
+    }
+    peer_finish();
+  };
+  if (R == 1) {
+    if (peer) peer_combine();
+    return;
+  }
   // Replicas: publish this slice, count arrivals; the last replica to arrive
   // merges all R slices (in replica order) and resets the counter.
   if (tid < 2 * G) slot[tid] = hdr[tid];
@@ -951,7 +1074,10 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   int* last = scratch + 127;
   if (tid == 0) *last = atomicAdd(&p.rep_cnt[bh * C + crank], 1) == R - 1 ? 1 : 0;
   __syncthreads();
-  if (!*last) return;
+  if (!*last) {
+    if (peer) peer_finish();
+    return;
+  }
   __threadfence();
   const float* base = p.rep_part + (size_t(bh) * R * C + crank) * RSZ;  // replica rr at + rr*C*RSZ
   for (int idx = e0 + tid; idx < e1; idx += kThreads) {
@@ -970,6 +1096,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     emit(idx, M, Ls, O);
   }
   if (tid == 0) p.rep_cnt[bh * C + crank] = 0;
+  if (peer) peer_combine();
 }
 
 // LSE merge of P shard partials (rank order) into the output [B, Hq, D].

@@ -159,6 +159,41 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// ---------------------------------------------------------------------------
+// Flags between GPUs (peer memory over NVLink). A shard writes its data into
+// every shard's exchange area, fences at system scope and then releases a
+// flag word (the launch's epoch) in each area; a reader acquires its own
+// area's flag. Waits are bounded like the mbarrier waits, with a longer
+// limit because the peers' launches are only loosely aligned in time.
+// ---------------------------------------------------------------------------
+constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;  // 10 s
+constexpr int kErrPeerTimeout = 4;
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait until *flag has reached `epoch` (wrap-safe); false (and the error word
+// set) on timeout.
+__device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, int* err) {
+  if (int32_t(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (int32_t(ld_acquire_sys(flag) - epoch) >= 0) return true;
+    if ((it & 63u) == 0u) {
+      if (globaltimer() - t0 > kPeerWaitLimitNs) {
+        if (err) atomicOr(err, kErrPeerTimeout);
+        return false;
+      }
+      __nanosleep(100);
+    }
+  }
+}
+
 // Generic-proxy writes -> async-proxy (TMA) reads ordering.
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");

@@ -15,7 +15,8 @@ constexpr int kUnionMax = 8192;                 // candidates gathered for the f
 constexpr int kMaxTopK = 1023;                  // K (recent block excluded)
 constexpr int kAllKeysMax = 2048;               // candidates held whole by every CTA (bitonic top-K)
 
-enum Mode { MODE_FUSED = 0, MODE_CANDIDATES = 1, MODE_ATTEND = 2 };
+enum Mode { MODE_FUSED = 0, MODE_CANDIDATES = 1, MODE_ATTEND = 2, MODE_PEER = 3 };
+constexpr int kMaxShards = 8;                   // peer mode: shards (GPUs) exchanging over peer memory
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 

@@ -36,7 +36,9 @@ DTYPES = {"f32": 0, "f16": 1, "bf16": 2}
 EXPORTED = ["sd_abi_version", "sd_status_string", "sd_last_error", "sd_index_create", "sd_index_destroy",
             "sd_index_config", "sd_index_arrays", "sd_index_offset", "sd_index_copy", "sd_append", "sd_trim",
             "sd_set_offset", "sd_rebuild_summaries", "sd_decode", "sd_shard_candidates", "sd_shard_attend",
-            "sd_shard_merge", "sd_check_device", "sd_set_launch_overlap", "sd_decode_noalloc"]
+            "sd_shard_merge", "sd_check_device", "sd_set_launch_overlap", "sd_decode_noalloc", "sd_comm_create",
+            "sd_comm_handle", "sd_comm_open", "sd_comm_destroy", "sd_shard_decode"]
+COMM_HANDLE_BYTES = 128
 
 
 class SDError(RuntimeError):
@@ -96,6 +98,11 @@ def lib() -> ctypes.CDLL:
             "sd_set_launch_overlap": ([vp, i32], i32),
             "sd_decode_noalloc": ([ctypes.POINTER(SDConfig), ctypes.POINTER(SDArrays), i64, vp, f32, vp, vp, vp, vp],
                                   i32),
+            "sd_comm_create": ([vp, pp], i32),
+            "sd_comm_handle": ([vp, vp], i32),
+            "sd_comm_open": ([vp, vp], i32),
+            "sd_comm_destroy": ([vp], i32),
+            "sd_shard_decode": ([vp, vp, vp, vp, vp, f32, vp, vp, vp], i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -284,6 +291,18 @@ class SparseIndex:
     def shard_merge(self, all_part_ml, all_part_o, out, stream=None) -> None:
         _check(lib().sd_shard_merge(self._h, _ptr(all_part_ml), _ptr(all_part_o), _ptr(out), _stream(stream)))
 
+    def shard_decode(self, comm: "ShardComm", q, k_new=None, v_new=None, scale: Optional[float] = None, out=None,
+                     sel_out=None, stream=None):
+        """One fused sequence-sharded decode step over peer memory (see
+        ShardComm); every shard calls it with the same arguments and gets the
+        full output."""
+        import torch
+        scale = 1.0 / math.sqrt(self.D) if scale is None else scale
+        out = torch.empty_like(q) if out is None else out
+        _check(lib().sd_shard_decode(self._h, comm._h, _ptr(q), _ptr(k_new), _ptr(v_new), scale, _ptr(out),
+                                     _ptr(sel_out), _stream(stream)))
+        return out
+
     def set_launch_overlap(self, enable: bool = True) -> None:
         """Let decode launches overlap the previous kernel on the stream
         (programmatic dependent launch); see sd_set_launch_overlap."""
@@ -295,7 +314,58 @@ class SparseIndex:
         return f.value
 
 
-def sharded_decode(index, q, k_new=None, v_new=None, scale=None, group=None, sel_out=None):
+class ShardComm:
+    """This shard's exchange area for the fused sharded step (sd_comm*).
+
+    Created from an index (any index of the same configuration can use it);
+    the shards' handles are exchanged with an all-gather over `group` (or by
+    `exchange(my_handle_bytes) -> all handles in shard order`), then opened.
+    Every shard must construct it at the same point of its program. `close()`
+    waits at a barrier of the group before the area is freed, because the
+    other shards map it."""
+
+    def __init__(self, index: "SparseIndex", group=None, exchange=None):
+        h = ctypes.c_void_p()
+        _check(lib().sd_comm_create(index._h, ctypes.byref(h)))
+        self._h = h
+        self.P = index.P
+        self.group = group
+        buf = (ctypes.c_uint8 * COMM_HANDLE_BYTES)()
+        _check(lib().sd_comm_handle(self._h, buf))
+        mine = bytes(buf)
+        if self.P == 1:
+            handles = mine
+        elif exchange is not None:
+            handles = exchange(mine)
+        else:
+            handles = _all_gather_bytes(mine, group)
+        if len(handles) != self.P * COMM_HANDLE_BYTES:
+            raise ValueError(f"expected {self.P} handles of {COMM_HANDLE_BYTES} bytes")
+        _check(lib().sd_comm_open(self._h, handles))
+
+    def close(self, barrier: bool = True) -> None:
+        if self._h is not None:
+            if barrier and self.P > 1:
+                import torch
+                import torch.distributed as dist
+                torch.cuda.synchronize()
+                dist.barrier(group=self.group)
+            lib().sd_comm_destroy(self._h)
+            self._h = None
+
+
+def _all_gather_bytes(data: bytes, group=None) -> bytes:
+    import torch
+    import torch.distributed as dist
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" else "cpu"
+    mine = torch.tensor(list(data), dtype=torch.uint8, device=dev)
+    world = dist.get_world_size(group)
+    allb = torch.empty(world * len(data), dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(allb, mine, group=group)
+    return bytes(allb.cpu().tolist())
+
+
+def sharded_decode(index, q, k_new=None, v_new=None, scale=None, group=None, sel_out=None, comm=None):
     """Sequence-sharded decode step over torch.distributed (NCCL over NVLink):
     local candidates -> all-gather -> global top-K + local attention ->
     all-gather of (m, l, o) partials -> log-sum-exp merge. Every rank calls it
@@ -303,9 +373,13 @@ def sharded_decode(index, q, k_new=None, v_new=None, scale=None, group=None, sel
 
     `index` is a SparseIndex (or anything with its shard_* methods and P, B,
     Hq, Hkv, D, K attributes). The gathers use flat views, the form that every
-    torch.distributed backend accepts."""
+    torch.distributed backend accepts. With `comm` (a ShardComm) the whole
+    step is one fused launch per shard that exchanges through peer memory
+    instead (SparseIndex.shard_decode)."""
     import torch
     import torch.distributed as dist
+    if comm is not None:
+        return index.shard_decode(comm, q, k_new, v_new, scale, sel_out=sel_out)
     P, BH, K = index.P, index.B * index.Hkv, index.K
     BQ, D = index.B * index.Hq, index.D
     dev = q.device

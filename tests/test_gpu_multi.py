@@ -1,7 +1,9 @@
 """Sequence-sharded decode across real GPUs (one process per GPU, NCCL): the
 output of `sparse_decode.sharded_decode` on every rank matches the oracle and
-the selection is the single-device one. Needs at least two GPUs; skipped
-otherwise."""
+the selection is the single-device one, through NCCL all-gathers and through
+the fused peer-memory step (ShardComm), which must give the same bits. The
+multi-GPU case needs at least two GPUs and is skipped otherwise; the fused
+step with a single shard runs on one GPU."""
 from __future__ import annotations
 
 import socket
@@ -25,7 +27,7 @@ def _rank_main(rank: int, world: int, port: int, results):
     import torch.distributed as dist
     from gpu_cases import to_dev, to_host
     from _util import host_case, rel_err
-    from sparse_decode import SparseIndex, sharded_decode
+    from sparse_decode import ShardComm, SparseIndex, sharded_decode
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
@@ -48,6 +50,17 @@ def _rank_main(rank: int, world: int, port: int, results):
                 outs.append(to_host(out, w.dtype))
                 sels.append(sel.cpu().numpy()[:, : w.n_sel])
                 assert idx.trim(1) == 1
+            # the fused peer-memory step: the same selection, the same output bits
+            comm = ShardComm(idx)
+            for rep in range(2):
+                sel = torch.full((B * Hkv, w.K + 1), -7, dtype=torch.int32, device="cuda")
+                out = sharded_decode(idx, q, k[:, :, T - 1].contiguous(), v[:, :, T - 1].contiguous(), c["scale"],
+                                     sel_out=sel, comm=comm)
+                torch.cuda.synchronize()
+                outs.append(to_host(out, w.dtype))
+                sels.append(sel.cpu().numpy()[:, : w.n_sel])
+                assert idx.trim(1) == 1
+            comm.close()
             res.append((outs, sels, idx.check_device()))
             idx.close()
         results.put((rank, res))
@@ -100,3 +113,58 @@ def test_sharded_decode_across_gpus(cuda, world):
                 if ref_out is None:
                     ref_out = o
                 assert np.array_equal(o, ref_out), (w.name, r)  # identical on every rank and step
+
+
+def test_peer_step_single_shard_matches_decode(cuda):
+    """The fused peer-memory step with one shard (the exchange goes to the
+    shard's own area): bit-identical to sd_decode over several steps, also
+    when the steps of three layers are replayed from a CUDA graph (the epoch
+    lives on the device)."""
+    import torch
+    from gpu_cases import to_dev
+    from _util import host_case
+    from sparse_decode import ShardComm, SparseIndex
+    w = Workload("peer1", B=1, Hq=32, Hkv=8, D=128, T=64 * 50 + 5, S=64, K=16, dtype="bf16", needles=4)
+    cases = [host_case(w, 400 + i) for i in range(3)]
+    B, Hkv, T, D = w.B, w.Hkv, w.T, w.D
+
+    def make(c):
+        idx = SparseIndex(B, w.Hq, Hkv, D, w.S, w.K, T, w.dtype, 0)
+        k = to_dev(c["ks"].reshape(B, Hkv, T, D), w.dtype)
+        v = to_dev(c["vs"].reshape(B, Hkv, T, D), w.dtype)
+        idx.append(k[:, :, : T - 1].contiguous(), v[:, :, : T - 1].contiguous())
+        return idx, to_dev(c["qs"], w.dtype), k[:, :, T - 1].contiguous(), v[:, :, T - 1].contiguous()
+
+    ref, peer = [make(c) for c in cases], [make(c) for c in cases]
+    comm = ShardComm(peer[0][0])
+    want = []
+    for (idx, q, kn, vn), c in zip(ref, cases):
+        want.append(idx.decode(q, kn, vn, c["scale"]).clone())
+        idx.trim(1)
+    outs = [torch.empty_like(q) for (_, q, _, _) in peer]
+    sels = [torch.empty((B * Hkv, w.K + 1), dtype=torch.int32, device="cuda") for _ in peer]
+    for rep in range(2):  # eager launches
+        for (idx, q, kn, vn), c, o, s in zip(peer, cases, outs, sels):
+            idx.shard_decode(comm, q, kn, vn, c["scale"], out=o, sel_out=s)
+            idx.trim(1)
+        torch.cuda.synchronize()
+        for o, wnt, s, c in zip(outs, want, sels, cases):
+            assert torch.equal(o, wnt)
+            assert np.array_equal(s.cpu().numpy()[:, : w.n_sel], c["sel"])
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for (idx, q, kn, vn), c, o in zip(peer, cases, outs):
+            idx.shard_decode(comm, q, kn, vn, c["scale"], out=o)
+    for (idx, _, _, _) in peer:
+        idx.trim(1)
+    for rep in range(3):
+        for o in outs:
+            o.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        for o, wnt in zip(outs, want):
+            assert torch.equal(o, wnt)
+    for (idx, _, _, _) in peer:
+        assert idx.check_device() == 0
+    del g
+    comm.close()
