@@ -183,6 +183,13 @@ typedef struct sd_comm sd_comm; /* opaque */
 int32_t sd_comm_create(const sd_index* idx, sd_comm** out);
 int32_t sd_comm_handle(const sd_comm* comm, void* handle);
 int32_t sd_comm_open(sd_comm* comm, const void* handles);
+/* Shards driven by one process (one GPU each, or several on one GPU for
+ * tests that run a single shard): open with every shard's comm, in shard
+ * order, instead of IPC handles; peer access between the devices is enabled
+ * here. */
+int32_t sd_comm_open_local(sd_comm* comm, sd_comm* const* shards);
+/* Bound of the kernel's waits for other shards (default 10 s; 1 ms .. 600 s). */
+int32_t sd_comm_set_wait_limit(sd_comm* comm, int64_t limit_ns);
 int32_t sd_comm_destroy(sd_comm* comm);
 int32_t sd_shard_decode(sd_index* idx, sd_comm* comm, const void* q, const void* k_new, const void* v_new,
                         float scale, void* out, int32_t* sel_out, sd_stream stream);

@@ -129,10 +129,12 @@ struct sd_comm {
   int P, pr, BH, K, C, R, G, D, RS;
   int resident;                     // every cluster of a launch fits on the GPU at once
   size_t bytes;
-  int64_t off_fpart, off_cand, off_part, off_ctl;
+  int64_t off_cand, off_part, off_ctl;
   uint8_t* local;
   uint8_t* peers[sd::kMaxShards];   // own area at [pr]
   bool opened;
+  bool ipc[sd::kMaxShards];         // peers[r] was opened from an IPC handle
+  uint64_t wait_ns;                 // bound of the kernel's waits for other shards
 };
 
 namespace {
@@ -298,10 +300,10 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   p.pdl_early = (overlap && other_before) ? 1 : 0;
   if (mode == sd::MODE_PEER) {
     for (int r = 0; r < comm->P; ++r) p.peer[r] = comm->peers[r];
-    p.x_fpart = comm->off_fpart;
     p.x_cand = comm->off_cand;
     p.x_part = comm->off_part;
     p.x_ctl = comm->off_ctl;
+    p.peer_wait_ns = comm->wait_ns;
   }
   const int64_t ncand = p.NB - 1;
   const int64_t nloc = ncand > p.pr ? (ncand - p.pr + p.P - 1) / p.P : 0;
@@ -644,6 +646,29 @@ int32_t sd_shard_merge(sd_index* x, const float* all_ml, const float* all_o, voi
 }
 
 namespace {
+// Shards of one process on different GPUs: let this comm's device access
+// every other shard's device (already-enabled access is fine).
+int32_t enable_peer_access(const sd_comm* m, sd_comm* const* shards) {
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return fail(SD_ERR_CUDA, "cudaGetDevice failed");
+  for (int r = 0; r < m->P; ++r) {
+    const int d = shards[r]->device;
+    if (d == m->device) continue;
+    int ok = 0;
+    cudaDeviceCanAccessPeer(&ok, m->device, d);
+    if (!ok) return fail(SD_ERR_CUDA, "device %d cannot access device %d", m->device, d);
+    cudaSetDevice(m->device);
+    cudaError_t e = cudaDeviceEnablePeerAccess(d, 0);
+    cudaSetDevice(cur);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+      cudaGetLastError();
+    } else if (e != cudaSuccess) {
+      return fail(SD_ERR_CUDA, "cudaDeviceEnablePeerAccess(%d -> %d): %s", m->device, d, cudaGetErrorString(e));
+    }
+  }
+  return SD_OK;
+}
+
 struct CommHandle {
   cudaIpcMemHandle_t ipc;
   int32_t magic, version, P, pr, BH, K, C, R, G, D;
@@ -666,10 +691,9 @@ int32_t sd_comm_create(const sd_index* x, sd_comm** out) {
   m.RS = 2 * m.G + (m.G * m.D + m.C - 1) / m.C;
   m.resident = max_active_clusters(x, x->C) >= int64_t(m.BH) * x->R ? 1 : 0;
   const int64_t P = m.P, BH = m.BH;
-  m.off_fpart = int64_t(align256(size_t(P * BH * 4)));
-  m.off_cand = m.off_fpart + int64_t(align256(size_t(P * BH * m.C * 4)));
-  m.off_part = m.off_cand + int64_t(align256(size_t(P * BH * std::max(m.K, 1) * 8)));
-  m.off_ctl = m.off_part + int64_t(align256(size_t(P * BH * m.C * m.RS * 4)));
+  m.off_cand = 0;
+  m.off_part = m.off_cand + int64_t(align256(size_t(P * BH * std::max(m.K, 1) * 2 * 8)));
+  m.off_ctl = m.off_part + int64_t(align256(size_t(P * BH * m.C * m.RS * 8)));
   m.bytes = size_t(m.off_ctl) + 256;
   int dev = 0;
   SD_CUDA(cudaGetDevice(&dev));
@@ -684,6 +708,7 @@ int32_t sd_comm_create(const sd_index* x, sd_comm** out) {
   }
   m.peers[m.pr] = m.local;
   m.opened = m.P == 1;
+  m.wait_ns = sd::kPeerWaitLimitNs;
   *out = new sd_comm(m);
   return SD_OK;
 }
@@ -724,12 +749,43 @@ int32_t sd_comm_open(sd_comm* m, const void* handles) {
     cudaError_t e = cudaIpcOpenMemHandle(&ptr, h.ipc, cudaIpcMemLazyEnablePeerAccess);
     if (e != cudaSuccess) {
       for (int q = 0; q < r; ++q)
-        if (q != m->pr && m->peers[q]) { cudaIpcCloseMemHandle(m->peers[q]); m->peers[q] = nullptr; }
+        if (q != m->pr && m->peers[q]) {
+          cudaIpcCloseMemHandle(m->peers[q]);
+          m->peers[q] = nullptr;
+          m->ipc[q] = false;
+        }
       return fail(SD_ERR_CUDA, "cudaIpcOpenMemHandle(shard %d) failed: %s", r, cudaGetErrorString(e));
     }
     m->peers[r] = static_cast<uint8_t*>(ptr);
+    m->ipc[r] = true;
   }
   m->opened = true;
+  return SD_OK;
+}
+
+int32_t sd_comm_open_local(sd_comm* m, sd_comm* const* shards) {
+  if (!m || !shards) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  if (m->opened) return m->P == 1 ? SD_OK : fail(SD_ERR_STATE, "comm is already open");
+  for (int r = 0; r < m->P; ++r) {
+    const sd_comm* o = shards[r];
+    if (!o) return fail(SD_ERR_INVALID_ARG, "shard %d's comm is NULL", r);
+    if (o->pr != r || o->P != m->P)
+      return fail(SD_ERR_INVALID_ARG, "comm %d belongs to shard %d of %d (expected %d of %d)", r, o->pr, o->P, r, m->P);
+    if (o->BH != m->BH || o->K != m->K || o->C != m->C || o->R != m->R || o->G != m->G || o->D != m->D ||
+        o->bytes != m->bytes)
+      return fail(SD_ERR_SHAPE, "shard %d's index configuration differs from this one's", r);
+  }
+  if (enable_peer_access(m, shards) != SD_OK) return SD_ERR_CUDA;
+  for (int r = 0; r < m->P; ++r) m->peers[r] = shards[r]->local;
+  m->opened = true;
+  return SD_OK;
+}
+
+int32_t sd_comm_set_wait_limit(sd_comm* m, int64_t limit_ns) {
+  if (!m) return fail(SD_ERR_INVALID_ARG, "NULL comm");
+  if (limit_ns < 1000000 || limit_ns > 600000000000ll)
+    return fail(SD_ERR_INVALID_ARG, "wait limit must be in [1 ms, 600 s] (got %lld ns)", (long long)limit_ns);
+  m->wait_ns = uint64_t(limit_ns);
   return SD_OK;
 }
 
@@ -737,7 +793,7 @@ int32_t sd_comm_destroy(sd_comm* m) {
   if (!m) return SD_OK;
   cudaError_t e = cudaSuccess;
   for (int r = 0; r < m->P; ++r)
-    if (r != m->pr && m->peers[r]) {
+    if (r != m->pr && m->peers[r] && m->ipc[r]) {
       cudaError_t e2 = cudaIpcCloseMemHandle(m->peers[r]);
       if (e == cudaSuccess) e = e2;
     }

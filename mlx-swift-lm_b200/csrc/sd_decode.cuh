@@ -774,39 +774,47 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
         scratch);
     select_union(U);
   } else if (peer && K > 0) {
-    // Peer mode: (1) this shard's local top-K goes into every shard's
-    // exchange area (0-padded full keys) and the group's flag is released
-    // there; (2) the group waits for every shard's flag in its own area;
-    // (3) the top-K of the P*K union, identical on every shard.
+    // Peer mode: (1) this shard's local top-K (0-padded full keys, two
+    // message words each) goes into every shard's exchange area; (2) every
+    // shard's candidates of the group are read from this shard's area as
+    // their words arrive; (3) the top-K of the P*K union, identical on every
+    // shard.
     const int BHn = int(gridDim.y);
     if (crank == 0 && rep == 0) {
       for (int r = 0; r < P; ++r) {
         unsigned long long* dst =
-            reinterpret_cast<unsigned long long*>(p.peer[r] + p.x_cand) + (size_t(pr) * BHn + bh) * K;
-        for (int i = tid; i < K; i += kThreads) dst[i] = i < kk ? full_key(pick[i].x, int(pick[i].y)) : 0ull;
-      }
-      __threadfence_system();
-      __syncthreads();
-      if (tid < P) {
-        __threadfence_system();
-        st_release_sys(reinterpret_cast<uint32_t*>(p.peer[tid]) + pr * BHn + bh, epoch);
+            reinterpret_cast<unsigned long long*>(p.peer[r] + p.x_cand) + (size_t(pr) * BHn + bh) * K * 2;
+        for (int i = tid; i < K; i += kThreads) {
+          const unsigned long long x = i < kk ? full_key(pick[i].x, int(pick[i].y)) : 0ull;
+          st_msg(dst + 2 * i, uint32_t(x >> 32), epoch);
+          st_msg(dst + 2 * i + 1, uint32_t(x), epoch);
+        }
       }
     }
-    if (tid == 0) {
-      const uint32_t* fl = reinterpret_cast<const uint32_t*>(p.peer[pr]);
-      for (int r = 0; r < P; ++r)
-        if (!wait_epoch(fl + r * BHn + bh, epoch, p.err)) break;
-    }
-    __syncthreads();
-    const unsigned long long* ck = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_cand) + size_t(bh) * K;
-    const size_t rstride = size_t(BHn) * K;
-    auto ckey = [&](int i) -> unsigned long long { return __ldcg(ck + size_t(i / K) * rstride + (i % K)); };
     const int N = P * K;
-    if (N <= kAllKeysMax && K <= 256) {
+    const bool small = N <= kAllKeysMax && K <= 256;
+    // small unions are staged in shared memory, clear of the runs and the pick list
+    unsigned long long* uk = reinterpret_cast<unsigned long long*>(sm + L.ring + 80 * 1024);
+    const unsigned long long* ck = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_cand);
+    auto cword = [&](int i) { return ck + ((size_t(i / K) * BHn + bh) * K + (i % K)) * 2; };
+    bool ok = true;
+    int nz = 0;
+    for (int i = tid; i < N; i += kThreads) {
+      const uint32_t hi = ld_msg(cword(i), epoch, p.peer_wait_ns, p.err, &ok);
+      const uint32_t lo = ld_msg(cword(i) + 1, epoch, p.peer_wait_ns, p.err, &ok);
+      const unsigned long long x = (static_cast<unsigned long long>(hi) << 32) | lo;
+      if (small) uk[i] = x;
+      nz += x != 0ull;
+    }
+    const int U = __syncthreads_count(nz > 0) > 0 ? N : 0;  // any candidate at all
+    if (U == 0) {
+      kk = 0;
+    } else if (small) {
       unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 32 * 1024);
-      if (K <= 64) block_topk<2>(ckey, N, runs, lane, warp, kThreads / 32);
-      else if (K <= 128) block_topk<4>(ckey, N, runs, lane, warp, kThreads / 32);
-      else block_topk<8>(ckey, N, runs, lane, warp, kThreads / 32);
+      auto ukey = [&](int i) -> unsigned long long { return uk[i]; };
+      if (K <= 64) block_topk<2>(ukey, N, runs, lane, warp, kThreads / 32);
+      else if (K <= 128) block_topk<4>(ukey, N, runs, lane, warp, kThreads / 32);
+      else block_topk<8>(ukey, N, runs, lane, warp, kThreads / 32);
       kk = __syncthreads_count(tid < K && runs[tid] != 0ull);
       for (int i = tid; i < kk; i += kThreads) {
         const unsigned long long x = runs[i];
@@ -814,17 +822,21 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       }
       __syncthreads();
     } else {
-      const int U = cta_compact(
-          N, [&](int i) { return ckey(i) != 0ull; },
+      // larger unions: the words have arrived; compact the non-zero keys into
+      // the ring's union area straight from the exchange area
+      auto gkey = [&](int i) {
+        return (ld_msg_raw(cword(i)) << 32) | (ld_msg_raw(cword(i) + 1) & 0xffffffffull);
+      };
+      const int Uc = cta_compact(
+          N, [&](int i) { return gkey(i) != 0ull; },
           [&](int pos, int i) {
-            const unsigned long long x = ckey(i);
+            const unsigned long long x = gkey(i);
             uni[pos] = make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x));
           },
           scratch);
-      select_union(U);
+      select_union(Uc);
     }
   }
-
   if (p.mode == MODE_CANDIDATES) {
     if (crank == 0 && rep == 0) {
       for (int i = tid; i < K; i += kThreads) {
@@ -966,13 +978,16 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     if (p.mode == MODE_FUSED) {
       static_cast<E*>(p.out)[bq * D + d] = Elt<E>::from_f32(Ls > 0.0f ? O / Ls : 0.0f);
     } else if (peer) {
-      // this shard's record of (group, slice) -- [2G (m, l)][slice of o] --
-      // into every shard's exchange area
+      // this shard's record of (group, slice) -- [2G (m, l)][slice of o] as
+      // message words -- into every shard's exchange area
       const size_t ro = ((size_t(pr) * gridDim.y + bh) * C + crank) * RS;
       for (int r = 0; r < P; ++r) {
-        float* rec = reinterpret_cast<float*>(p.peer[r] + p.x_part) + ro;
-        rec[2 * G + idx - e0] = O;
-        if (idx == e0 || d == 0) { rec[g] = M; rec[G + g] = Ls; }
+        unsigned long long* rec = reinterpret_cast<unsigned long long*>(p.peer[r] + p.x_part) + ro;
+        st_msg(rec + 2 * G + idx - e0, __float_as_uint(O), epoch);
+        if (idx == e0 || d == 0) {
+          st_msg(rec + g, __float_as_uint(M), epoch);
+          st_msg(rec + G + g, __float_as_uint(Ls), epoch);
+        }
       }
     } else {
       p.part_o[bq * D + d] = O;
@@ -1025,36 +1040,33 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       }
     }
   };
-  // Peer mode, after this shard's record of the slice went out: release the
-  // slice's flag in every area, wait for every shard's record of it here, and
-  // merge them in shard order (the same output on every shard).
+  // Peer mode, after this shard's record of the slice went out: read every
+  // shard's record of it from this shard's area as its words arrive and merge
+  // them in shard order (the same output on every shard).
   auto peer_combine = [&]() {
     const int BHn = int(gridDim.y);
-    __threadfence_system();
-    __syncthreads();
-    if (tid < P) {
-      __threadfence_system();
-      st_release_sys(reinterpret_cast<uint32_t*>(p.peer[tid] + p.x_fpart) + (size_t(pr) * BHn + bh) * C + crank,
-                     epoch);
-    }
-    if (tid == 0) {
-      const uint32_t* fl = reinterpret_cast<const uint32_t*>(p.peer[pr] + p.x_fpart);
-      for (int r = 0; r < P; ++r)
-        if (!wait_epoch(fl + (size_t(r) * BHn + bh) * C + crank, epoch, p.err)) break;
-    }
-    __syncthreads();
-    const float* recs = reinterpret_cast<const float*>(p.peer[pr] + p.x_part);
+    const unsigned long long* recs = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_part);
     auto rec = [&](int r) { return recs + ((size_t(r) * BHn + bh) * C + crank) * RS; };
+    float* hm = reinterpret_cast<float*>(sm + L.cpart);  // [P][2G] (m, l) of every shard
+    bool ok = true;
+    const int g0 = e0 / D, g1 = (e1 - 1) / D;  // heads this slice touches (the records hold only those)
+    __syncthreads();  // cpart may still be read by the slice loop
+    for (int i = tid; i < P * 2 * G; i += kThreads) {
+      const int k = i % (2 * G), g = k % G;
+      if (e1 > e0 && g >= g0 && g <= g1)
+        hm[i] = __uint_as_float(ld_msg(rec(i / (2 * G)) + k, epoch, p.peer_wait_ns, p.err, &ok));
+    }
+    __syncthreads();
     for (int idx = e0 + tid; idx < e1; idx += kThreads) {
       const int g = idx / D, d = idx % D;
       float M = -INFINITY;
-      for (int r = 0; r < P; ++r) M = fmaxf(M, __ldcg(rec(r) + g));
+      for (int r = 0; r < P; ++r) M = fmaxf(M, hm[r * 2 * G + g]);
       float Ls = 0.0f, O = 0.0f;
       if (M != -INFINITY) {
         for (int r = 0; r < P; ++r) {
-          const float f = exp2f(__ldcg(rec(r) + g) - M);
-          Ls += __ldcg(rec(r) + G + g) * f;
-          O += __ldcg(rec(r) + 2 * G + idx - e0) * f;
+          const float f = exp2f(hm[r * 2 * G + g] - M);
+          Ls += hm[r * 2 * G + G + g] * f;
+          O += __uint_as_float(ld_msg(rec(r) + 2 * G + idx - e0, epoch, p.peer_wait_ns, p.err, &ok)) * f;
         }
       }
       const size_t bq = size_t(b) * p.Hq + size_t(h) * G + g;

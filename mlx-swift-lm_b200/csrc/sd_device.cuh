@@ -160,36 +160,40 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // ---------------------------------------------------------------------------
-// Flags between GPUs (peer memory over NVLink). A shard writes its data into
-// every shard's exchange area, fences at system scope and then releases a
-// flag word (the launch's epoch) in each area; a reader acquires its own
-// area's flag. Waits are bounded like the mbarrier waits, with a longer
-// limit because the peers' launches are only loosely aligned in time.
+// Messages between GPUs (peer memory over NVLink). Every 8-byte word carries
+// 32 bits of payload and the launch's epoch: an aligned 8-byte store is
+// single-copy atomic, so a reader that sees the current epoch in a word also
+// sees that word's payload, with no fence and no separate flag (one NVLink
+// trip per message). Waits are bounded like the mbarrier waits, with a
+// longer, configurable limit because the shards' launches are only loosely
+// aligned in time.
 // ---------------------------------------------------------------------------
-constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;  // 10 s
 constexpr int kErrPeerTimeout = 4;
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_msg(unsigned long long* p, uint32_t payload, uint32_t epoch) {
+  const unsigned long long v = (static_cast<unsigned long long>(epoch) << 32) | payload;
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_msg_raw(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-// Wait until *flag has reached `epoch` (wrap-safe); false (and the error word
-// set) on timeout.
-__device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, int* err) {
-  if (int32_t(ld_acquire_sys(flag) - epoch) >= 0) return true;
+// The payload of a message word once it carries `epoch`; on expiry of
+// limit_ns the error word is set, *ok cleared, and 0 returned.
+__device__ __forceinline__ uint32_t ld_msg(const unsigned long long* p, uint32_t epoch, uint64_t limit_ns, int* err,
+                                           bool* ok) {
+  unsigned long long v = ld_msg_raw(p);
+  if (uint32_t(v >> 32) == epoch) return uint32_t(v);
+  if (!*ok) return 0u;
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
-    if (int32_t(ld_acquire_sys(flag) - epoch) >= 0) return true;
-    if ((it & 63u) == 0u) {
-      if (globaltimer() - t0 > kPeerWaitLimitNs) {
-        if (err) atomicOr(err, kErrPeerTimeout);
-        return false;
-      }
-      __nanosleep(100);
+    v = ld_msg_raw(p);
+    if (uint32_t(v >> 32) == epoch) return uint32_t(v);
+    if ((it & 15u) == 0u && globaltimer() - t0 > limit_ns) {
+      if (err) atomicOr(err, kErrPeerTimeout);
+      *ok = false;
+      return 0u;
     }
   }
 }

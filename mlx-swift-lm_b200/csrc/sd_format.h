@@ -17,6 +17,7 @@ constexpr int kAllKeysMax = 2048;               // candidates held whole by ever
 
 enum Mode { MODE_FUSED = 0, MODE_CANDIDATES = 1, MODE_ATTEND = 2, MODE_PEER = 3 };
 constexpr int kMaxShards = 8;                   // peer mode: shards (GPUs) exchanging over peer memory
+constexpr unsigned long long kPeerWaitLimitNs = 10000000000ull;  // peer mode: default bound of a wait (10 s)
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 

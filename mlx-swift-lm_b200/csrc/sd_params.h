@@ -43,13 +43,14 @@ struct DecodeParams {
   float* racc_out;        // [BH, D] the same sum after the appended row
   int racc_rebuild;       // 1: racc_in is not valid; sum the recent block's rows from the cache
   // Peer mode: every shard's exchange area mapped into this process (own at
-  // [pr]). Area layout, identical on every shard:
-  //   [P][BH] u32 candidate flags | [P][BH][C] u32 partial flags |
-  //   [P][BH][K] u64 candidate keys (at x_cand) | [P][BH][C][RSZ] f32 partial
-  //   records (at x_part) | 2 u32 control words of this shard (at x_ctl):
-  //   the last finished epoch and the count of finished CTAs.
+  // [pr]). Area layout, identical on every shard, all message words (32-bit
+  // payload | epoch << 32): [P][BH][K][2] candidate keys (hi, lo) at x_cand,
+  // [P][BH][C][RSZ] partial records ([2G] (m, l), then the slice of o) at
+  // x_part; at x_ctl two u32 control words of this shard: the last finished
+  // epoch and the count of finished CTAs.
   uint8_t* peer[8];
-  int64_t x_fpart, x_cand, x_part, x_ctl;  // byte offsets inside an area
+  int64_t x_cand, x_part, x_ctl;  // byte offsets inside an area
+  uint64_t peer_wait_ns;                   // bound of every wait for another shard
 };
 
 struct AppendParams {

@@ -37,7 +37,8 @@ EXPORTED = ["sd_abi_version", "sd_status_string", "sd_last_error", "sd_index_cre
             "sd_index_config", "sd_index_arrays", "sd_index_offset", "sd_index_copy", "sd_append", "sd_trim",
             "sd_set_offset", "sd_rebuild_summaries", "sd_decode", "sd_shard_candidates", "sd_shard_attend",
             "sd_shard_merge", "sd_check_device", "sd_set_launch_overlap", "sd_decode_noalloc", "sd_comm_create",
-            "sd_comm_handle", "sd_comm_open", "sd_comm_destroy", "sd_shard_decode"]
+            "sd_comm_handle", "sd_comm_open", "sd_comm_open_local", "sd_comm_set_wait_limit", "sd_comm_destroy",
+            "sd_shard_decode"]
 COMM_HANDLE_BYTES = 128
 
 
@@ -101,6 +102,8 @@ def lib() -> ctypes.CDLL:
             "sd_comm_create": ([vp, pp], i32),
             "sd_comm_handle": ([vp, vp], i32),
             "sd_comm_open": ([vp, vp], i32),
+            "sd_comm_open_local": ([vp, ctypes.POINTER(ctypes.c_void_p)], i32),
+            "sd_comm_set_wait_limit": ([vp, i64], i32),
             "sd_comm_destroy": ([vp], i32),
             "sd_shard_decode": ([vp, vp, vp, vp, vp, f32, vp, vp, vp], i32),
         }
@@ -324,12 +327,15 @@ class ShardComm:
     waits at a barrier of the group before the area is freed, because the
     other shards map it."""
 
-    def __init__(self, index: "SparseIndex", group=None, exchange=None):
+    def __init__(self, index: "SparseIndex", group=None, exchange=None, local: bool = False):
         h = ctypes.c_void_p()
         _check(lib().sd_comm_create(index._h, ctypes.byref(h)))
         self._h = h
         self.P = index.P
         self.group = group
+        self.local = local
+        if local:  # opened later with open_local (shards of this process)
+            return
         buf = (ctypes.c_uint8 * COMM_HANDLE_BYTES)()
         _check(lib().sd_comm_handle(self._h, buf))
         mine = bytes(buf)
@@ -343,9 +349,19 @@ class ShardComm:
             raise ValueError(f"expected {self.P} handles of {COMM_HANDLE_BYTES} bytes")
         _check(lib().sd_comm_open(self._h, handles))
 
+    @staticmethod
+    def open_local(comms) -> None:
+        """Open the comms of all shards driven by this process (shard order)."""
+        arr = (ctypes.c_void_p * len(comms))(*[c._h.value for c in comms])
+        for c in comms:
+            _check(lib().sd_comm_open_local(c._h, arr))
+
+    def set_wait_limit(self, seconds: float) -> None:
+        _check(lib().sd_comm_set_wait_limit(self._h, int(seconds * 1e9)))
+
     def close(self, barrier: bool = True) -> None:
         if self._h is not None:
-            if barrier and self.P > 1:
+            if barrier and self.P > 1 and not self.local:
                 import torch
                 import torch.distributed as dist
                 torch.cuda.synchronize()

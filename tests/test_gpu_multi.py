@@ -115,6 +115,44 @@ def test_sharded_decode_across_gpus(cuda, world):
                 assert np.array_equal(o, ref_out), (w.name, r)  # identical on every rank and step
 
 
+def test_peer_wait_expires_without_the_other_shard(cuda):
+    """Failure detection of the fused sharded step: shard 0 of 2 runs alone
+    (shard 1's kernel is never launched, so its flags are never set). Both of
+    the kernel's waits for shard 1 give up after the comm's limit, the error
+    bit 4 is reported, and the GPU context stays usable."""
+    import time
+    import torch
+    from gpu_cases import to_dev
+    from _util import host_case
+    from sparse_decode import ShardComm, SparseIndex
+    w = Workload("lonely", B=1, Hq=8, Hkv=2, D=128, T=64 * 20 + 3, S=64, K=4, dtype="bf16", needles=1)
+    c = host_case(w, 500)
+    B, Hkv, T, D = w.B, w.Hkv, w.T, w.D
+    shards = [SparseIndex(B, w.Hq, Hkv, D, w.S, w.K, T, w.dtype, 0, shard_rank=r, shard_count=2) for r in range(2)]
+    comms = [ShardComm(s, local=True) for s in shards]
+    ShardComm.open_local(comms)
+    comms[0].set_wait_limit(0.2)
+    k = to_dev(c["ks"].reshape(B, Hkv, T, D), w.dtype)
+    v = to_dev(c["vs"].reshape(B, Hkv, T, D), w.dtype)
+    q = to_dev(c["qs"], w.dtype)
+    shards[0].append(k[:, :, : T - 1].contiguous(), v[:, :, : T - 1].contiguous())
+    torch.cuda.synchronize()
+    t0 = time.time()
+    shards[0].shard_decode(comms[0], q)
+    torch.cuda.synchronize()
+    dt = time.time() - t0
+    assert shards[0].check_device() & 4
+    assert 0.3 < dt < 5.0, dt  # two expired waits of 0.2 s
+    # the context still works
+    one = SparseIndex(B, w.Hq, Hkv, D, w.S, w.K, T, w.dtype, 0)
+    one.append(k[:, :, : T - 1].contiguous(), v[:, :, : T - 1].contiguous())
+    one.decode(q, k[:, :, T - 1].contiguous(), v[:, :, T - 1].contiguous(), c["scale"])
+    torch.cuda.synchronize()
+    assert one.check_device() == 0
+    for cm in comms:
+        cm.close()
+
+
 def test_peer_step_single_shard_matches_decode(cuda):
     """The fused peer-memory step with one shard (the exchange goes to the
     shard's own area): bit-identical to sd_decode over several steps, also
