@@ -109,8 +109,8 @@ struct sd_index {
   void* arena;
   size_t arena_bytes;
   void *k_data, *v_data, *k_scales, *k_biases, *v_scales, *v_biases, *summ;
-  float* rep_part;      // R > 1: replica partials; rep_cnt: arrival counters
-  int* rep_cnt;
+  unsigned long long* gslot;  // C*R > 1: the group merge's message words
+  uint32_t* gep;        // C*R > 1: epoch of each group's last merged launch
   float* racc;          // 2 x [BH, D] running sums of the recent block's rows
   int racc_cur;         // buffer holding the current sums
   bool racc_valid;      // the current buffer matches the cache
@@ -291,8 +291,8 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
     p.racc_rebuild = x->racc_valid ? 0 : 1;
   }
   p.R = x->R;
-  p.rep_part = x->rep_part;
-  p.rep_cnt = x->rep_cnt;
+  p.gslot = x->gslot;
+  p.gep = x->gep;
   const bool other_before = note_stream(st, x);
   // Peer mode never overlaps launches: the exchange areas are reused by the
   // next launch only after this one has finished everywhere.
@@ -433,8 +433,9 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
   const size_t sb = c.kv_bits ? align256(size_t(BH) * x->cap_local * x->groups * x->esize) : 0;
   const size_t su = align256(size_t(BH) * x->nb_local * c.head_dim * x->esize);
   const int GD = x->G * c.head_dim;
-  const size_t rp = x->R > 1 ? align256(size_t(BH) * x->R * x->C * (2 * x->G + (GD + x->C - 1) / x->C) * 4) : 0;
-  const size_t rcn = x->R > 1 ? align256(size_t(BH) * x->C * 4) : 0;
+  const int Q = x->C * x->R;
+  const size_t rp = Q > 1 ? align256(size_t(BH) * Q * Q * (2 * x->G + (GD + Q - 1) / Q) * 8) : 0;
+  const size_t rcn = Q > 1 ? align256(size_t(BH) * 4) : 0;
   const size_t ra = align256(size_t(2) * BH * c.head_dim * 4);
   x->arena_bytes = 2 * kv + 4 * sb + su + rp + rcn + ra + 256;
   cudaError_t e = cudaMalloc(&x->arena, x->arena_bytes);
@@ -452,8 +453,8 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
     x->v_biases = a; a += sb;
   }
   x->summ = a; a += su;
-  x->rep_part = rp ? reinterpret_cast<float*>(a) : nullptr; a += rp;
-  x->rep_cnt = rcn ? reinterpret_cast<int*>(a) : nullptr; a += rcn;
+  x->gslot = rp ? reinterpret_cast<unsigned long long*>(a) : nullptr; a += rp;
+  x->gep = rcn ? reinterpret_cast<uint32_t*>(a) : nullptr; a += rcn;
   x->racc = reinterpret_cast<float*>(a); a += ra;
   x->d_err = reinterpret_cast<int*>(a);
   e = cudaMemset(x->arena, 0, x->arena_bytes);
@@ -688,12 +689,13 @@ int32_t sd_comm_create(const sd_index* x, sd_comm** out) {
   m.device = x->device;
   m.P = c.shard_count; m.pr = c.shard_rank;
   m.BH = c.batch * c.n_kv_heads; m.K = c.top_k; m.C = x->C; m.R = x->R; m.G = x->G; m.D = c.head_dim;
-  m.RS = 2 * m.G + (m.G * m.D + m.C - 1) / m.C;
+  const int Q = m.C * m.R;
+  m.RS = 2 * m.G + (m.G * m.D + Q - 1) / Q;
   m.resident = max_active_clusters(x, x->C) >= int64_t(m.BH) * x->R ? 1 : 0;
   const int64_t P = m.P, BH = m.BH;
   m.off_cand = 0;
   m.off_part = m.off_cand + int64_t(align256(size_t(P * BH * std::max(m.K, 1) * 2 * 8)));
-  m.off_ctl = m.off_part + int64_t(align256(size_t(P * BH * m.C * m.RS * 8)));
+  m.off_ctl = m.off_part + int64_t(align256(size_t(P * BH * Q * m.RS * 8)));
   m.bytes = size_t(m.off_ctl) + 256;
   int dev = 0;
   SD_CUDA(cudaGetDevice(&dev));
@@ -933,25 +935,27 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   if (rc == SD_OK) rc = choose_cluster(&x);
   if (rc != SD_OK) return rc;
 
-  // Scratch layout: [0, 256) error word, then the arrival counters, then the
-  // replica partials. Fewer replicas are used if the partials do not fit;
-  // with one replica only the counters and the error word remain.
+  // Scratch layout: [0, 256) error word, then the groups' epochs, then the
+  // group merge's message words. Fewer replicas are used if the words do not
+  // fit. Both regions are cleared by every call (the array is shared by calls
+  // of any configuration, and a word left by another configuration could
+  // carry a matching epoch).
   const int GD = x.G * c.head_dim;
-  auto part_bytes = [&](int R) {
-    return R > 1 ? size_t(BH) * R * x.C * (2 * x.G + (GD + x.C - 1) / x.C) * 4 : size_t(0);
+  auto slot_bytes = [&](int R) {
+    const int Q = x.C * R;
+    return Q > 1 ? size_t(BH) * Q * Q * (2 * x.G + (GD + Q - 1) / Q) * 8 : size_t(0);
   };
-  const size_t cnt_bytes = align256(size_t(BH) * x.C * 4);
-  while (x.R > 1 && 256 + cnt_bytes + part_bytes(x.R) > kNoAllocScratch) --x.R;
-  if (256 + cnt_bytes + part_bytes(x.R) > kNoAllocScratch)
+  const size_t ep_bytes = align256(size_t(BH) * 4);
+  while (x.R > 1 && 256 + ep_bytes + slot_bytes(x.R) > kNoAllocScratch) --x.R;
+  if (256 + ep_bytes + slot_bytes(x.R) > kNoAllocScratch)
     return fail(SD_ERR_CAPACITY, "batch*kv_heads (%lld) needs %zu bytes of scratch; the limit is %zu",
-                (long long)BH, 256 + cnt_bytes, kNoAllocScratch);
+                (long long)BH, 256 + ep_bytes + slot_bytes(x.R), kNoAllocScratch);
   void* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc != SD_OK) return rc;
   uint8_t* sb = static_cast<uint8_t*>(scratch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // the error word and the arrival counters must start at zero
-  SD_CUDA(cudaMemsetAsync(sb, 0, 256 + cnt_bytes, st));
+  SD_CUDA(cudaMemsetAsync(sb, 0, 256 + ep_bytes + slot_bytes(x.R), st));
 
   x.k_data = arrays->k_data; x.v_data = arrays->v_data;
   x.k_scales = arrays->k_scales; x.k_biases = arrays->k_biases;
@@ -980,8 +984,8 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   p.sel_out = sel_out;
   p.err = device_flags ? device_flags : reinterpret_cast<int*>(sb);
   p.R = x.R;
-  p.rep_cnt = reinterpret_cast<int*>(sb + 256);
-  p.rep_part = x.R > 1 ? reinterpret_cast<float*>(sb + 256 + cnt_bytes) : nullptr;
+  p.gep = reinterpret_cast<uint32_t*>(sb + 256);
+  p.gslot = x.C * x.R > 1 ? reinterpret_cast<unsigned long long*>(sb + 256 + ep_bytes) : nullptr;
   const int64_t nloc = p.NB - 1;
   if ((nloc + x.C - 1) / x.C > sd::kLocalKeysMax)
     return fail(SD_ERR_SHAPE, "too many blocks per CTA for cluster size %d", x.C);

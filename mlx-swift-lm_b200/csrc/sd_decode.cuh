@@ -437,6 +437,9 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   // new token, and this index unless pdl_early says otherwise) is read only
   // after griddep_wait.
   if (tid == 0) griddep_launch_dependents();
+  // Cluster start-up barrier: arrived here, waited for before the first key
+  // is pushed into a peer's shared memory.
+  if (C > 1) cluster_arrive_relaxed();
   if (!p.pdl_early) griddep_wait();
   if (tid == 0) {
     for (int s = 0; s < F::kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
@@ -459,29 +462,48 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   const int c0 = chunk_lo(crank), c1 = chunk_lo(crank + 1);
   const int n = c1 - c0;
   auto jglob = [&](int i) { return (c0 + i) * P + pr; };
-  // Up to kAllKeysMax candidates: every CTA gathers all keys of the group and
-  // selects by a block-wide bitonic top-K (no second exchange).
-  const bool whole = p.mode != MODE_ATTEND && nloc <= kAllKeysMax && K <= 256;
+  // Up to kAllKeysMax candidates: each CTA scores its chunk and pushes the
+  // keys into every cluster peer's copy of the group's key array; after one
+  // cluster barrier every CTA selects by the same block-wide bitonic top-K.
+  const bool whole = p.mode != MODE_ATTEND && nloc <= kAllKeysMax && K <= 128;
   uint32_t* allk = reinterpret_cast<uint32_t*>(sm + L.allk);
   if (whole) keys = allk + c0;
+  const int sc0 = c0, sn = n;  // the rows this CTA scores
 
   // Score-phase loads go out before the query barrier so that the two memory
   // latencies overlap. Warps 0..7 score; the producer warp does not.
-  constexpr int LPB = F::kSumLanes, EPC = F::kSumEpc, BPW = 32 / LPB, UNR = 4, NWS = kConsumerWarps;
+  constexpr int LPB = F::kSumLanes, EPC = F::kSumEpc, BPW = 32 / LPB, UNR = 8, NWS = kConsumerWarps;
   const int sub = lane / LPB, cch = lane % LPB;
   const bool scorer = warp < NWS && p.mode != MODE_ATTEND;
   const uint8_t* srow0 =
-      static_cast<const uint8_t*>(p.summ) + (size_t(bh) * p.nb_stride + c0) * D * sizeof(E) + cch * 16;
+      static_cast<const uint8_t*>(p.summ) + (size_t(bh) * p.nb_stride + sc0) * D * sizeof(E) + cch * 16;
   uint4 raw[UNR];
   if (scorer) {
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
       const int i = warp * BPW + u * NWS * BPW + sub;
-      raw[u] = i < n ? ldg_stream(srow0 + size_t(i) * D * sizeof(E)) : make_uint4(0u, 0u, 0u, 0u);
+      raw[u] = i < sn ? ldg_stream(srow0 + size_t(i) * D * sizeof(E)) : make_uint4(0u, 0u, 0u, 0u);
     }
   }
 
   if (p.pdl_early) griddep_wait();
+  // The producer warp appends the new token during phase 1; its inputs are
+  // loaded now, next to the queries.
+  constexpr int EPL = D / 32;
+  TokenRows<E, BITS, D> tok;
+  float rin[EPL];
+  const int apos = (T - 1) % S;  // position of the new token in its block
+  const bool keep_sums = appending && rep == 0;
+  if (warp == kConsumerWarps && appending) {
+    append_load<E, BITS, D>(tok, static_cast<const E*>(p.k_new) + size_t(bh) * D,
+                            static_cast<const E*>(p.v_new) + size_t(bh) * D, lane);
+    if (keep_sums && apos > 0 && !p.racc_rebuild) {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) rin[e] = p.racc_in[size_t(bh) * D + lane * EPL + e];
+    }
+  }
+  // this launch's epoch of the group merge (the previous launch is complete)
+  const uint32_t gep = (Q > 1 && p.mode != MODE_CANDIDATES) ? __ldcg(p.gep + bh) + 1u : 0u;
   const E* qg = static_cast<const E*>(p.q) + (size_t(b) * p.Hq + size_t(h) * G) * D;
   for (int i = tid; i < G * D; i += kThreads) {
     const int g = i / D, d = i % D;
@@ -492,36 +514,6 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
 #pragma unroll
     for (int g = 1; g < G; ++g) a = __fadd_rn(a, Elt<E>::to_f32(qg[g * D + tid]));
     qsum[tid] = a;
-  }
-  // Running column sums of the recent block (fp32, rows in order -- the
-  // canonical summary order): acc = acc_before + appended row; when the
-  // appended row fills the block, its summary key is acc / S. One CTA per
-  // group (the appender of replica 0) keeps them.
-  if (appending && rep == 0 && tid < D) {
-    const int d = tid, pos = (T - 1) % S;
-    const size_t row0 = size_t(bh) * p.cap_local + size_t((NB - 1) / P) * S;
-    const float v = appended_value<E, BITS, D>(static_cast<const E*>(p.k_new) + size_t(bh) * D, d);
-    float acc = v;
-    if (pos > 0) {
-      const float before = p.racc_rebuild ? column_sum<E, BITS, D>(p.k_data, p.k_scales, p.k_biases, row0, pos, d)
-                                          : p.racc_in[size_t(bh) * D + d];
-      acc = __fadd_rn(before, v);
-    }
-    p.racc_out[size_t(bh) * D + d] = acc;
-    if (completing)
-      static_cast<E*>(p.summ)[(size_t(bh) * p.nb_stride + (NB - 1) / P) * D + d] =
-          Elt<E>::from_f32(__fdiv_rn(acc, float(S)));
-  }
-  if (appending && warp < 2) {
-    const int t = T - 1;
-    const size_t row = size_t(bh) * p.cap_local + size_t((NB - 1) / P) * S + (t % S);
-    if (warp == 0)
-      write_token_row<E, BITS, D>(static_cast<const E*>(p.k_new) + size_t(bh) * D, p.k_data, p.k_scales,
-                                  p.k_biases, row, lane);
-    else
-      write_token_row<E, BITS, D>(static_cast<const E*>(p.v_new) + size_t(bh) * D, p.v_data, p.v_scales,
-                                  p.v_biases, row, lane);
-    fence_proxy_async_global();
   }
   __syncthreads();
   if constexpr (BITS != 0) {
@@ -534,20 +526,53 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   }
 
   // ---------------- phase 1: block scores ----------------
+  // (the producer warp appends the new token meanwhile)
+  if (C > 1) cluster_wait();
+  if (warp == kConsumerWarps && appending) {
+    // The token's K and V rows; every replica cluster writes them (the same
+    // bytes) so that its own TMA loads are ordered after the write by the
+    // proxy fence here and a barrier of its own before the loads.
+    const size_t row0 = size_t(bh) * p.cap_local + size_t((NB - 1) / P) * S;
+    float kdeq[EPL];
+    append_store<E, BITS, D>(tok, p.k_data, p.k_scales, p.k_biases, p.v_data, p.v_scales, p.v_biases, row0 + apos,
+                             lane, kdeq);
+    fence_proxy_async_global();
+    // Running column sums of the recent block (fp32, rows in order -- the
+    // canonical summary order): acc = acc_before + appended row as stored;
+    // when the appended row fills the block, its summary key is acc / S. One
+    // CTA per group (the appender of replica 0) keeps them.
+    if (keep_sums) {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const int d = lane * EPL + e;
+        float acc = kdeq[e];
+        if (apos > 0) {
+          const float before = p.racc_rebuild
+                                   ? column_sum<E, BITS, D>(p.k_data, p.k_scales, p.k_biases, row0, apos, d)
+                                   : rin[e];
+          acc = __fadd_rn(before, kdeq[e]);
+        }
+        p.racc_out[size_t(bh) * D + d] = acc;
+        if (completing)
+          static_cast<E*>(p.summ)[(size_t(bh) * p.nb_stride + (NB - 1) / P) * D + d] =
+              Elt<E>::from_f32(__fdiv_rn(acc, float(S)));
+      }
+    }
+  }
   if (scorer) {
     float qr[EPC];
 #pragma unroll
     for (int e = 0; e < EPC; ++e) qr[e] = qsum[cch * EPC + e];
-    for (int it = warp * BPW; it < n; it += NWS * BPW * UNR) {
+    for (int it = warp * BPW; it < sn; it += NWS * BPW * UNR) {
       uint4 cur[UNR];
 #pragma unroll
       for (int u = 0; u < UNR; ++u) cur[u] = raw[u];
       const int nx = it + NWS * BPW * UNR;
-      if (nx < n) {
+      if (nx < sn) {
 #pragma unroll
         for (int u = 0; u < UNR; ++u) {
           const int i = nx + u * NWS * BPW + sub;
-          raw[u] = i < n ? ldg_stream(srow0 + size_t(i) * D * sizeof(E)) : make_uint4(0u, 0u, 0u, 0u);
+          raw[u] = i < sn ? ldg_stream(srow0 + size_t(i) * D * sizeof(E)) : make_uint4(0u, 0u, 0u, 0u);
         }
       }
 #pragma unroll
@@ -563,49 +588,36 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
         for (int e = 0; e < EPC; ++e) a = __fmaf_rn(qr[e], f[e], a);
 #pragma unroll
         for (int o = LPB / 2; o >= 1; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-        if (cch == 0 && i < n) {
+        if (cch == 0 && i < sn) {
           const float sc = __fmul_rn(a, p.scale);
           keys[i] = score_key(sc);
-          if (p.scores_out) p.scores_out[size_t(bh) * NB + size_t(c0 + i) * P + pr] = sc;
+          if (p.scores_out) p.scores_out[size_t(bh) * NB + size_t(sc0 + i) * P + pr] = sc;
         }
       }
     }
   }
   __syncthreads();
 
+  // This CTA's keys into every cluster peer's copy of the group's key array.
+  if (whole && C > 1) {
+    for (int idx = tid; idx < n * (C - 1); idx += kThreads) {
+      const int i = idx % n, rr = idx / n, r = rr < crank ? rr : rr + 1;
+      st_cluster_u32(map_rank(smem_u32(keys + i), uint32_t(r)), keys[i]);
+    }
+  }
+
   // ---------------- phase 2: selection ----------------
   int kk;  // blocks chosen by top-K
   if (whole) {
-    if (C > 1) {
-      cluster_sync();
-      const uint32_t ab = smem_u32(allk);
-      for (int ib = tid; ib < nloc; ib += kThreads * 4) {
-        uint32_t val[4];
-        int at[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int i = ib + k * kThreads;
-          at[k] = -1;
-          if (i < nloc && (i < c0 || i >= c1)) {
-            at[k] = i;
-            val[k] = ld_cluster_u32(map_rank(ab + uint32_t(i) * 4u, uint32_t(((i + 1) * C - 1) / nloc)));
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if (at[k] >= 0) allk[at[k]] = val[k];
-      }
-      __syncthreads();
-    }
+    if (C > 1) cluster_sync();  // every peer's pushed keys have landed
     kk = min(K, nloc);
-    auto akey = [&](int i) -> unsigned long long { return full_key(allk[i], i * P + pr); };
     if (nloc <= K || K == 0) {
       for (int i = tid; i < kk; i += kThreads) pick[i] = make_uint2(allk[i], uint32_t(i * P + pr));
     } else {
       unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 32 * 1024);
+      auto akey = [&](int i) -> unsigned long long { return full_key(allk[i], i * P + pr); };
       if (K <= 64) block_topk<2>(akey, nloc, runs, lane, warp, kThreads / 32);
-      else if (K <= 128) block_topk<4>(akey, nloc, runs, lane, warp, kThreads / 32);
-      else block_topk<8>(akey, nloc, runs, lane, warp, kThreads / 32);
+      else block_topk<4>(akey, nloc, runs, lane, warp, kThreads / 32);
       for (int i = tid; i < kk; i += kThreads) {
         const unsigned long long x = runs[i];
         pick[i] = make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x));
@@ -792,7 +804,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       }
     }
     const int N = P * K;
-    const bool small = N <= kAllKeysMax && K <= 256;
+    const bool small = N <= kAllKeysMax && K <= 128;
     // small unions are staged in shared memory, clear of the runs and the pick list
     unsigned long long* uk = reinterpret_cast<unsigned long long*>(sm + L.ring + 80 * 1024);
     const unsigned long long* ck = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_cand);
@@ -813,8 +825,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 32 * 1024);
       auto ukey = [&](int i) -> unsigned long long { return uk[i]; };
       if (K <= 64) block_topk<2>(ukey, N, runs, lane, warp, kThreads / 32);
-      else if (K <= 128) block_topk<4>(ukey, N, runs, lane, warp, kThreads / 32);
-      else block_topk<8>(ukey, N, runs, lane, warp, kThreads / 32);
+      else block_topk<4>(ukey, N, runs, lane, warp, kThreads / 32);
       kk = __syncthreads_count(tid < K && runs[tid] != 0ull);
       for (int i = tid; i < kk; i += kThreads) {
         const unsigned long long x = runs[i];
@@ -845,7 +856,6 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
         p.cand_block[size_t(bh) * K + i] = v ? int32_t(pick[i].y) : -1;
       }
     }
-    if (whole && C > 1) cluster_sync();  // peers may still be reading this CTA's keys
     return;
   }
 
@@ -951,27 +961,18 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     if (d == 0) { cpart[g] = M; cpart[G + g] = Ls; }
     cpart[2 * G + g * D + d] = O;
   }
-  // Push this CTA's partial to the CTA that owns each output element (and
-  // (m, l) to everyone), one cluster barrier, then merge from local memory.
+  // The group's Q = C*R CTAs merge through L2: output elements are cut into Q
+  // slices, CTA q owns slice q. Every CTA sends each owner a record -- the
+  // (m, l) of every head, then its partial o over the owner's slice -- as
+  // message words tagged with the group's launch epoch; each owner reads the
+  // Q records of its slice as their words arrive and merges them in CTA
+  // order. All Q CTAs are resident at once (clusters, or replica clusters
+  // chosen so that all fit), so the owners' bounded waits always end.
   constexpr int GD = G * D;
-  const int RS = 2 * G + (GD + C - 1) / C;  // per-source stride of the receive buffer
-  float* recv = reinterpret_cast<float*>(sm + L.recv);
-  auto e_lo = [&](int r) { return r * GD / C; };
-  __syncthreads();
-  if (C > 1) {
-    const uint32_t ra = smem_u32(recv) + uint32_t(crank * RS) * 4u;
-    for (int idx = tid; idx < GD; idx += kThreads) {
-      const int owner = (idx * C + C - 1) / GD;
-      st_cluster_u32(map_rank(ra + uint32_t(2 * G + idx - e_lo(owner)) * 4u, uint32_t(owner)),
-                     __float_as_uint(cpart[2 * G + idx]));
-    }
-    for (int idx = tid; idx < C * 2 * G; idx += kThreads) {
-      const int r = idx / (2 * G), k = idx % (2 * G);
-      st_cluster_u32(map_rank(ra + uint32_t(k) * 4u, uint32_t(r)), __float_as_uint(cpart[k]));
-    }
-    cluster_sync();
-  }
-  const int e0 = e_lo(crank), e1 = e_lo(crank + 1);
+  const int SL = (GD + Q - 1) / Q;   // slice length
+  const int RS = 2 * G + SL;          // record length (words)
+  const int e0 = min(GD, qrank * SL), e1 = min(GD, e0 + SL);
+  const int g0 = e0 / D, g1 = (e1 - 1) / D;  // heads this slice touches
   auto emit = [&](int idx, float M, float Ls, float O) {
     const int g = idx / D, d = idx % D;
     const size_t bq = size_t(b) * p.Hq + size_t(h) * G + g;
@@ -980,7 +981,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     } else if (peer) {
       // this shard's record of (group, slice) -- [2G (m, l)][slice of o] as
       // message words -- into every shard's exchange area
-      const size_t ro = ((size_t(pr) * gridDim.y + bh) * C + crank) * RS;
+      const size_t ro = ((size_t(pr) * gridDim.y + bh) * Q + qrank) * RS;
       for (int r = 0; r < P; ++r) {
         unsigned long long* rec = reinterpret_cast<unsigned long long*>(p.peer[r] + p.x_part) + ro;
         st_msg(rec + 2 * G + idx - e0, __float_as_uint(O), epoch);
@@ -994,41 +995,91 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       if (d == 0) { p.part_ml[bq * 2] = M; p.part_ml[bq * 2 + 1] = Ls; }
     }
   };
-  // this cluster's (M, L) per head, from the partials pushed above
-  float* hdr = reinterpret_cast<float*>(scratch);  // [2G] floats (G <= 8); the scan area is free here
-  if (tid < G) {
-    float M = -INFINITY;
-    for (int r = 0; r < C; ++r) M = fmaxf(M, C > 1 ? recv[r * RS + tid] : cpart[tid]);
-    float Ls = 0.0f;
-    if (M != -INFINITY)
-      for (int r = 0; r < C; ++r) {
-        const float mr = C > 1 ? recv[r * RS + tid] : cpart[tid];
-        Ls += (C > 1 ? recv[r * RS + G + tid] : cpart[G + tid]) * exp2f(mr - M);
-      }
-    hdr[tid] = M;
-    hdr[G + tid] = Ls;
-  }
-  __syncthreads();
-  // replica slot of this CTA's slice: [2G header][slice]
-  const int RSZ = 2 * G + (GD + C - 1) / C;
-  float* slot = R > 1 ? p.rep_part + ((size_t(bh) * R + rep) * C + crank) * RSZ : nullptr;
-  for (int idx = e0 + tid; idx < e1; idx += kThreads) {
-    const int g = idx / D;
-    const float M = hdr[g];
-    float O = 0.0f;
-    if (M != -INFINITY) {
-      for (int r = 0; r < C; ++r) {
-        const float mr = C > 1 ? recv[r * RS + g] : cpart[g];
-        const float orr = C > 1 ? recv[r * RS + 2 * G + idx - e0] : cpart[2 * G + idx];
-        O += orr * exp2f(mr - M);
-      }
+  __syncthreads();  // cpart is complete
+  if (Q == 1) {
+    for (int idx = e0 + tid; idx < e1; idx += kThreads) {
+      const int g = idx / D;
+      emit(idx, cpart[g], cpart[G + g], cpart[2 * G + idx]);
     }
-    if (R == 1) emit(idx, M, hdr[G + g], O);
-    else slot[2 * G + idx - e0] = O;
+  } else {
+    unsigned long long* slots = p.gslot + size_t(bh) * Q * Q * RS;  // [owner][source][RS]
+    for (int i = tid; i < Q * RS; i += kThreads) {
+      const int o = i / RS, k = i - o * RS;
+      const int e = o * SL + (k - 2 * G);
+      if (k >= 2 * G && e >= GD) continue;
+      st_msg_gpu(slots + (size_t(o) * Q + qrank) * RS + k, __float_as_uint(k < 2 * G ? cpart[k] : cpart[2 * G + e]),
+                 gep);
+    }
+    // as the owner of [e0, e1): every source's record, gathered into shared
+    // memory with all loads of a batch in flight at once (the ring is free)
+    const unsigned long long* mine = slots + size_t(qrank) * Q * RS;
+    float* rq = reinterpret_cast<float*>(sm + L.ring);  // [Q][RS]
+    const int nw = e1 - e0;
+    auto needed = [&](int k) {
+      if (k >= 2 * G) return k - 2 * G < nw;
+      const int g = k % G;
+      return nw > 0 && g >= g0 && g <= g1;
+    };
+    gather_msgs<false>([&](int i) { return mine + i; }, Q * RS, gep, kWaitLimitNs, p.err, rq, tid, kThreads,
+                       [&](int i) { return needed(i % RS); });
+    __syncthreads();
+    for (int idx = e0 + tid; idx < e1; idx += kThreads) {
+      const int g = idx / D;
+      float M = -INFINITY;
+      for (int q = 0; q < Q; ++q) M = fmaxf(M, rq[q * RS + g]);
+      float Ls = 0.0f, O = 0.0f;
+      if (M != -INFINITY) {
+        for (int q = 0; q < Q; ++q) {
+          const float f = exp2f(rq[q * RS + g] - M);
+          Ls += rq[q * RS + G + g] * f;
+          O += rq[q * RS + 2 * G + idx - e0] * f;
+        }
+      }
+      emit(idx, M, Ls, O);
+    }
+    // Owner 0 has every CTA's record, so every CTA of the group has read the
+    // epoch: the next launch may use the next one.
+    __syncthreads();
+    if (qrank == 0 && tid == 0) p.gep[bh] = gep;
   }
-  // Peer mode: every CTA counts itself finished in its own area; the last one
-  // of the launch resets the count and publishes the epoch.
-  auto peer_finish = [&]() {
+  if (!peer) return;
+
+  // ---------------- peer mode: merge the shards ----------------
+  // After this shard's record of the slice went out: read every shard's
+  // record of it from this shard's area as its words arrive and merge them in
+  // shard order (the same output on every shard). Then every CTA counts
+  // itself finished in its own area; the last one of the launch resets the
+  // count and publishes the epoch.
+  {
+    const int BHn = int(gridDim.y);
+    const unsigned long long* recs = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_part);
+    auto rec = [&](int r) { return recs + ((size_t(r) * BHn + bh) * Q + qrank) * RS; };
+    float* rp = reinterpret_cast<float*>(sm + L.ring + 32 * 1024);  // [P][RS] (the ring is free)
+    const int nw = e1 - e0;
+    __syncthreads();  // the group merge above may still read the ring
+    gather_msgs<true>([&](int i) { return rec(i / RS) + (i % RS); }, P * RS, epoch, p.peer_wait_ns, p.err, rp, tid,
+                      kThreads, [&](int i) {
+                        const int k = i % RS;
+                        if (k >= 2 * G) return k - 2 * G < nw;
+                        const int g = k % G;
+                        return nw > 0 && g >= g0 && g <= g1;
+                      });
+    __syncthreads();
+    for (int idx = e0 + tid; idx < e1; idx += kThreads) {
+      const int g = idx / D, d = idx % D;
+      float M = -INFINITY;
+      for (int r = 0; r < P; ++r) M = fmaxf(M, rp[r * RS + g]);
+      float Ls = 0.0f, O = 0.0f;
+      if (M != -INFINITY) {
+        for (int r = 0; r < P; ++r) {
+          const float f = exp2f(rp[r * RS + g] - M);
+          Ls += rp[r * RS + G + g] * f;
+          O += rp[r * RS + 2 * G + idx - e0] * f;
+        }
+      }
+      const size_t bq = size_t(b) * p.Hq + size_t(h) * G + g;
+      static_cast<E*>(p.out)[bq * D + d] = Elt<E>::from_f32(Ls > 0.0f ? O / Ls : 0.0f);
+    }
     __syncthreads();
     if (tid == 0) {
       uint32_t* ctl = reinterpret_cast<uint32_t*>(p.peer[pr] + p.x_ctl);
@@ -1039,76 +1090,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
         ctl[0] = epoch;
       }
     }
-  };
-  // Peer mode, after this shard's record of the slice went out: read every
-  // shard's record of it from this shard's area as its words arrive and merge
-  // them in shard order (the same output on every shard).
-  auto peer_combine = [&]() {
-    const int BHn = int(gridDim.y);
-    const unsigned long long* recs = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_part);
-    auto rec = [&](int r) { return recs + ((size_t(r) * BHn + bh) * C + crank) * RS; };
-    float* hm = reinterpret_cast<float*>(sm + L.cpart);  // [P][2G] (m, l) of every shard
-    bool ok = true;
-    const int g0 = e0 / D, g1 = (e1 - 1) / D;  // heads this slice touches (the records hold only those)
-    __syncthreads();  // cpart may still be read by the slice loop
-    for (int i = tid; i < P * 2 * G; i += kThreads) {
-      const int k = i % (2 * G), g = k % G;
-      if (e1 > e0 && g >= g0 && g <= g1)
-        hm[i] = __uint_as_float(ld_msg(rec(i / (2 * G)) + k, epoch, p.peer_wait_ns, p.err, &ok));
-    }
-    __syncthreads();
-    for (int idx = e0 + tid; idx < e1; idx += kThreads) {
-      const int g = idx / D, d = idx % D;
-      float M = -INFINITY;
-      for (int r = 0; r < P; ++r) M = fmaxf(M, hm[r * 2 * G + g]);
-      float Ls = 0.0f, O = 0.0f;
-      if (M != -INFINITY) {
-        for (int r = 0; r < P; ++r) {
-          const float f = exp2f(hm[r * 2 * G + g] - M);
-          Ls += hm[r * 2 * G + G + g] * f;
-          O += __uint_as_float(ld_msg(rec(r) + 2 * G + idx - e0, epoch, p.peer_wait_ns, p.err, &ok)) * f;
-        }
-      }
-      const size_t bq = size_t(b) * p.Hq + size_t(h) * G + g;
-      static_cast<E*>(p.out)[bq * D + d] = Elt<E>::from_f32(Ls > 0.0f ? O / Ls : 0.0f);
-    }
-    peer_finish();
-  };
-  if (R == 1) {
-    if (peer) peer_combine();
-    return;
   }
-  // Replicas: publish this slice, count arrivals; the last replica to arrive
-  // merges all R slices (in replica order) and resets the counter.
-  if (tid < 2 * G) slot[tid] = hdr[tid];
-  __threadfence();
-  __syncthreads();
-  int* last = scratch + 127;
-  if (tid == 0) *last = atomicAdd(&p.rep_cnt[bh * C + crank], 1) == R - 1 ? 1 : 0;
-  __syncthreads();
-  if (!*last) {
-    if (peer) peer_finish();
-    return;
-  }
-  __threadfence();
-  const float* base = p.rep_part + (size_t(bh) * R * C + crank) * RSZ;  // replica rr at + rr*C*RSZ
-  for (int idx = e0 + tid; idx < e1; idx += kThreads) {
-    const int g = idx / D;
-    float M = -INFINITY;
-    for (int rr = 0; rr < R; ++rr) M = fmaxf(M, __ldcg(base + size_t(rr) * C * RSZ + g));
-    float Ls = 0.0f, O = 0.0f;
-    if (M != -INFINITY) {
-      for (int rr = 0; rr < R; ++rr) {
-        const float* sl = base + size_t(rr) * C * RSZ;
-        const float f = exp2f(__ldcg(sl + g) - M);
-        Ls += __ldcg(sl + G + g) * f;
-        O += __ldcg(sl + 2 * G + idx - e0) * f;
-      }
-    }
-    emit(idx, M, Ls, O);
-  }
-  if (tid == 0) p.rep_cnt[bh * C + crank] = 0;
-  if (peer) peer_combine();
 }
 
 // LSE merge of P shard partials (rank order) into the output [B, Hq, D].

@@ -179,6 +179,28 @@ __device__ __forceinline__ unsigned long long ld_msg_raw(const unsigned long lon
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// The same between the CTAs of one GPU (device scope).
+__device__ __forceinline__ void st_msg_gpu(unsigned long long* p, uint32_t payload, uint32_t epoch) {
+  const unsigned long long v = (static_cast<unsigned long long>(epoch) << 32) | payload;
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_msg_gpu(const unsigned long long* p, uint32_t epoch, uint64_t limit_ns,
+                                               int* err, bool* ok) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  if (uint32_t(v >> 32) == epoch) return uint32_t(v);
+  if (!*ok) return 0u;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    if (uint32_t(v >> 32) == epoch) return uint32_t(v);
+    if ((it & 15u) == 0u && globaltimer() - t0 > limit_ns) {
+      if (err) atomicOr(err, kErrTimeout);
+      *ok = false;
+      return 0u;
+    }
+  }
+}
 // The payload of a message word once it carries `epoch`; on expiry of
 // limit_ns the error word is set, *ok cleared, and 0 returned.
 __device__ __forceinline__ uint32_t ld_msg(const unsigned long long* p, uint32_t epoch, uint64_t limit_ns, int* err,
@@ -194,6 +216,57 @@ __device__ __forceinline__ uint32_t ld_msg(const unsigned long long* p, uint32_t
       if (err) atomicOr(err, kErrPeerTimeout);
       *ok = false;
       return 0u;
+    }
+  }
+}
+
+// Gather the payloads (as floats) of the message words w[i], i < n, for
+// which want(i) holds, into dst[i], with a batch of loads in flight per thread
+// before any is checked; words not yet carrying `epoch` are polled again
+// (bounded). All threads of the CTA call; the caller synchronises after.
+// kSys: the words are written by other GPUs (system scope) rather than by
+// other CTAs of this GPU.
+template <bool kSys, class Addr, class Want>
+__device__ __forceinline__ void gather_msgs(Addr addr, int n, uint32_t epoch, uint64_t limit_ns, int* err, float* dst,
+                                            int tid, int nthreads, Want want) {
+  constexpr int BATCH = 8;
+  for (int base = tid; base < n; base += nthreads * BATCH) {
+    bool need[BATCH];
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) need[j] = base + j * nthreads < n && want(base + j * nthreads);
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+      unsigned long long v[BATCH];
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j) {
+        v[j] = 0ull;
+        if (need[j]) {
+          if constexpr (kSys)
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v[j]) : "l"(addr(base + j * nthreads)) : "memory");
+          else
+            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v[j]) : "l"(addr(base + j * nthreads)) : "memory");
+        }
+      }
+      bool left = false;
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j) {
+        if (!need[j]) continue;
+        if (uint32_t(v[j] >> 32) == epoch) {
+          dst[base + j * nthreads] = __uint_as_float(uint32_t(v[j]));
+          need[j] = false;
+        } else {
+          left = true;
+        }
+      }
+      if (!left) break;
+      if (it == 0) t0 = globaltimer();
+      else if ((it & 15u) == 0u && globaltimer() - t0 > limit_ns) {
+        if (err) atomicOr(err, kSys ? kErrPeerTimeout : kErrTimeout);
+#pragma unroll
+        for (int j = 0; j < BATCH; ++j)
+          if (need[j]) dst[base + j * nthreads] = 0.0f;
+        break;
+      }
     }
   }
 }
@@ -297,6 +370,14 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Split cluster barrier: arrive early, wait right before the first access to
+// a peer's shared memory (every CTA of the cluster has started by then).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 // Address of the same shared variable in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t map_rank(uint32_t local_smem_addr, uint32_t rank) {

@@ -13,6 +13,7 @@ constexpr int kRingBytes = 160 * 1024;          // TMA ring; aliases the selecti
 constexpr int kLocalKeysMax = 16384;            // candidate blocks scored by one CTA
 constexpr int kUnionMax = 8192;                 // candidates gathered for the final top-K
 constexpr int kMaxTopK = 1023;                  // K (recent block excluded)
+constexpr int kMaxGroupCtas = 64;               // C * R: CTAs of one (b, kv-head) group
 constexpr int kAllKeysMax = 2048;               // candidates held whole by every CTA (bitonic top-K)
 
 enum Mode { MODE_FUSED = 0, MODE_CANDIDATES = 1, MODE_ATTEND = 2, MODE_PEER = 3 };
@@ -63,7 +64,7 @@ struct Layout {
   int scratch;     // 128 ints: scans [0,33), radix state [40,48), selection tables [64,112)
   int ps;          // per consumer warp: kTileTokens * G * groups floats
   int cpart;       // G*(D+2) floats: this CTA's merged (m, l, o)
-  int recv;        // partials pushed by the cluster for this CTA's output slice
+  int recv;        // (m, l) of every CTA of the group for this CTA's output slice
   int allk;        // kAllKeysMax u32: every candidate key of the group (bitonic top-K)
   int bars;        // 2 * 16 mbarriers
   int total;
@@ -83,7 +84,7 @@ __host__ __device__ inline Layout make_layout(int D, int G, int groups) {
   L.scratch = off; off += 128 * 4;
   L.ps = off; off += kConsumerWarps * align_up(kTileTokens * G * groups * 4, 16);
   L.cpart = off; off += align_up(G * (D + 2) * 4, 16);
-  L.recv = off; off += align_up((G * D + 16 + 2 * G * 16) * 4, 16);
+  L.recv = off; off += align_up(kMaxGroupCtas * 2 * G * 4, 16);
   L.allk = off; off += kAllKeysMax * 4;
   L.bars = off; off += 32 * 8;
   L.total = off;

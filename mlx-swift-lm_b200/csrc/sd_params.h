@@ -36,8 +36,8 @@ struct DecodeParams {
   float* part_o;          // attend mode: out [B*Hq, D] unnormalised
   int* err;               // device error word (sd::kErr*)
   int R;                  // replica clusters per (b, kv-head): each attends 1/R of the tiles
-  float* rep_part;        // R > 1: [BH, R, C, 2G + ceil(G*D/C)] partials of the replicas
-  int* rep_cnt;           // R > 1: [BH, C] arrival counters (zero between launches)
+  unsigned long long* gslot;  // Q = C*R > 1: [BH][Q owners][Q sources][2G + ceil(G*D/Q)] message words
+  uint32_t* gep;          // Q > 1: [BH] epoch of each group's last merged launch
   int pdl_early;          // 1: this index's summaries may be read before the grid-dependency wait
   const float* racc_in;   // [BH, D] fp32 sum of the recent block's rows before this step
   float* racc_out;        // [BH, D] the same sum after the appended row

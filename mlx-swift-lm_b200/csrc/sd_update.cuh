@@ -20,16 +20,14 @@ namespace sd {
 // little-endian in uint32 words). The fp32 operations match the CPU
 // restatement in oracle/sd_oracle.cpp (orc_quantize) one for one.
 template <typename E, int BITS, int D>
-__device__ __forceinline__ void quantize_row_warp(const E* src, uint32_t* wq, E* sc, E* bi, int lane) {
-  constexpr int EPL = D / 32;            // elements per lane
+__device__ __forceinline__ void quantize_row_regs(const float (&w)[D / 32], uint32_t* wq, E* sc, E* bi, int lane,
+                                                  float (&deq)[D / 32]) {
+  constexpr int EPL = D / 32;            // elements per lane (lane holds elements lane*EPL ..)
   constexpr int LPG = 64 / EPL;          // lanes per quantization group
   constexpr int PER_WORD = 32 / BITS;    // codes per uint32
   constexpr int LPW = PER_WORD / EPL;    // lanes sharing one word (>= 1)
   static_assert(EPL * BITS <= 32, "lane codes exceed one word");
   const float n_bins = float((1 << BITS) - 1);
-  float w[EPL];
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) w[e] = Elt<E>::to_f32(src[lane * EPL + e]);
   float wmax = w[0], wmin = w[0];
 #pragma unroll
   for (int e = 1; e < EPL; ++e) { wmax = fmaxf(wmax, w[e]); wmin = fminf(wmin, w[e]); }
@@ -45,12 +43,15 @@ __device__ __forceinline__ void quantize_row_warp(const E* src, uint32_t* wq, E*
   const float q0 = rintf(__fdiv_rn(edge, scale));
   if (q0 != 0.0f) scale = __fdiv_rn(edge, q0);
   const float bias = (q0 == 0.0f) ? 0.0f : edge;
+  // what a reader of the cache sees: the stored (rounded) scale and bias
+  const float s_st = Elt<E>::to_f32(Elt<E>::from_f32(scale)), b_st = Elt<E>::to_f32(Elt<E>::from_f32(bias));
   uint32_t bits = 0;
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
     float c = rintf(__fdiv_rn(__fsub_rn(w[e], bias), scale));
     c = fminf(fmaxf(c, 0.0f), n_bins);
     bits |= uint32_t(c) << (BITS * ((lane * EPL + e) % PER_WORD));
+    deq[e] = __fmaf_rn(s_st, c, b_st);
   }
 #pragma unroll
   for (int o = 1; o < LPW; o <<= 1) bits |= __shfl_xor_sync(0xffffffffu, bits, o);
@@ -61,6 +62,16 @@ __device__ __forceinline__ void quantize_row_warp(const E* src, uint32_t* wq, E*
     bi[g] = Elt<E>::from_f32(bias);
   }
 }
+
+template <typename E, int BITS, int D>
+__device__ __forceinline__ void quantize_row_warp(const E* src, uint32_t* wq, E* sc, E* bi, int lane) {
+  constexpr int EPL = D / 32;
+  float w[EPL], deq[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) w[e] = Elt<E>::to_f32(src[lane * EPL + e]);
+  quantize_row_regs<E, BITS, D>(w, wq, sc, bi, lane, deq);
+}
+
 
 // Element d of key row `row` as fp32 (dequantized with fma(scale, code, bias)).
 template <typename E, int BITS, int D>
@@ -115,35 +126,6 @@ __device__ __forceinline__ float column_sum(const void* data, const void* scales
   return acc;
 }
 
-// Element d of the appended key row as the cache stores it: the row itself
-// for dense caches; for 4/8-bit caches the dequantized code, found with the
-// same fp32 steps as quantize_row_warp (group min/max are order-free).
-template <typename E, int BITS, int D>
-__device__ __forceinline__ float appended_value(const E* row, int d) {
-  if constexpr (BITS == 0) {
-    return Elt<E>::to_f32(row[d]);
-  } else {
-    const float n_bins = float((1 << BITS) - 1);
-    const int g0 = (d / 64) * 64;
-    float wmax = -INFINITY, wmin = INFINITY;
-    for (int i = 0; i < 64; ++i) {
-      const float w = Elt<E>::to_f32(row[g0 + i]);
-      wmax = fmaxf(wmax, w);
-      wmin = fminf(wmin, w);
-    }
-    float scale = fmaxf(__fdiv_rn(__fsub_rn(wmax, wmin), n_bins), 1e-7f);
-    const bool mask = fabsf(wmin) > fabsf(wmax);
-    if (!mask) scale = -scale;
-    const float edge = mask ? wmin : wmax;
-    const float q0 = rintf(__fdiv_rn(edge, scale));
-    if (q0 != 0.0f) scale = __fdiv_rn(edge, q0);
-    const float bias = (q0 == 0.0f) ? 0.0f : edge;
-    float c = rintf(__fdiv_rn(__fsub_rn(Elt<E>::to_f32(row[d]), bias), scale));
-    c = fminf(fmaxf(c, 0.0f), n_bins);
-    return __fmaf_rn(Elt<E>::to_f32(Elt<E>::from_f32(scale)), c, Elt<E>::to_f32(Elt<E>::from_f32(bias)));
-  }
-}
-
 // Write one token row of K and V (warp 0: K, warp 1: V) at local row `row`.
 template <typename E, int BITS, int D>
 __device__ __forceinline__ void write_token_row(const E* src, void* data, void* scales, void* biases,
@@ -155,6 +137,49 @@ __device__ __forceinline__ void write_token_row(const E* src, void* data, void* 
     constexpr int WORDS = D * BITS / 32, NG = D / 64;
     quantize_row_warp<E, BITS, D>(src, static_cast<uint32_t*>(data) + row * WORDS,
                                   static_cast<E*>(scales) + row * NG, static_cast<E*>(biases) + row * NG, lane);
+  }
+}
+
+// The decode step's own token, one warp: the K and V rows arrive in registers
+// (loaded by append_load as early as possible), are stored (quantized for
+// 4/8-bit caches), and the returned key values are the row as the cache
+// holds it (dequantized codes for 4/8-bit) -- the input of the running sums.
+template <typename E, int BITS, int D>
+struct TokenRows {
+  float k[D / 32], v[D / 32];
+};
+template <typename E, int BITS, int D>
+__device__ __forceinline__ void append_load(TokenRows<E, BITS, D>& t, const E* k_src, const E* v_src, int lane) {
+  constexpr int EPL = D / 32;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    t.k[e] = Elt<E>::to_f32(k_src[lane * EPL + e]);
+    t.v[e] = Elt<E>::to_f32(v_src[lane * EPL + e]);
+  }
+}
+template <typename E, int BITS, int D>
+__device__ __forceinline__ void append_store(const TokenRows<E, BITS, D>& t, void* k_data, void* k_scales,
+                                             void* k_biases, void* v_data, void* v_scales, void* v_biases,
+                                             size_t row, int lane, float (&kdeq)[D / 32]) {
+  constexpr int EPL = D / 32;
+  if constexpr (BITS == 0) {
+    E* kd = static_cast<E*>(k_data) + row * D + lane * EPL;
+    E* vd = static_cast<E*>(v_data) + row * D + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      kd[e] = Elt<E>::from_f32(t.k[e]);
+      vd[e] = Elt<E>::from_f32(t.v[e]);
+      kdeq[e] = t.k[e];
+    }
+  } else {
+    constexpr int WORDS = D * BITS / 32, NG = D / 64;
+    float vdeq[EPL];
+    quantize_row_regs<E, BITS, D>(t.k, static_cast<uint32_t*>(k_data) + row * WORDS,
+                                  static_cast<E*>(k_scales) + row * NG, static_cast<E*>(k_biases) + row * NG, lane,
+                                  kdeq);
+    quantize_row_regs<E, BITS, D>(t.v, static_cast<uint32_t*>(v_data) + row * WORDS,
+                                  static_cast<E*>(v_scales) + row * NG, static_cast<E*>(v_biases) + row * NG, lane,
+                                  vdeq);
   }
 }
 
