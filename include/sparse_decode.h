@@ -222,15 +222,17 @@ int32_t sd_check_device(sd_index* idx, int32_t* flags, sd_stream stream);
  * call decodes one token (no append) like sd_decode. device_flags (nullable,
  * a caller-owned device int, zeroed by the caller) receives the same error
  * bits as sd_check_device reports.
- * The kernel's scratch (replica partials and arrival counters) lives in a
- * fixed array of SD_NOALLOC_SCRATCH_BYTES of device memory inside the
- * library, which every GPU that loads the library keeps until the process
+ * The kernel's scratch (the message words through which the CTAs of a
+ * (batch, kv-head) group merge their partial results, and the groups' epochs)
+ * lives in a fixed array of SD_NOALLOC_SCRATCH_BYTES of device memory inside
+ * the library, which every GPU that loads the library keeps until the process
  * exits. The first call on a device looks up that array's device address.
  * All calls on a device share the array and it keeps the last call's
- * contents (the call clears the parts that must start at zero), so two calls
- * that overlap on the GPU race with each other: serialise them. A
- * configuration whose scratch cannot fit (batch * n_kv_heads beyond about
- * 16k groups) is rejected with SD_ERR_CAPACITY. Single-shard caches only.
+ * contents (every call clears the part it uses), so two calls that overlap on
+ * the GPU race with each other: serialise them. When the scratch of the
+ * usual launch shape does not fit, fewer CTAs per group are used (down to
+ * one, which needs only the epochs); a configuration that still cannot fit
+ * is rejected with SD_ERR_CAPACITY. Single-shard caches only.
  * No counterpart in the reference. */
 #define SD_NOALLOC_SCRATCH_BYTES (1u << 20)
 int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arrays, int64_t offset, const void* q, float scale,

@@ -941,21 +941,29 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   // of any configuration, and a word left by another configuration could
   // carry a matching epoch).
   const int GD = x.G * c.head_dim;
-  auto slot_bytes = [&](int R) {
-    const int Q = x.C * R;
+  auto slot_bytes = [&](int C, int R) {
+    const int Q = C * R;
     return Q > 1 ? size_t(BH) * Q * Q * (2 * x.G + (GD + Q - 1) / Q) * 8 : size_t(0);
   };
   const size_t ep_bytes = align256(size_t(BH) * 4);
-  while (x.R > 1 && 256 + ep_bytes + slot_bytes(x.R) > kNoAllocScratch) --x.R;
-  if (256 + ep_bytes + slot_bytes(x.R) > kNoAllocScratch)
+  auto fits = [&]() { return 256 + ep_bytes + slot_bytes(x.C, x.R) <= kNoAllocScratch; };
+  // fewer replicas first, then smaller clusters (one CTA per group needs no message words)
+  while (!fits() && x.R > 1) --x.R;
+  while (!fits() && x.C > 1) {
+    int c2 = x.C - 1;
+    while (c2 > 1 && ((x.nb_local + c2 - 1) / c2 > sd::kLocalKeysMax || max_active_clusters(&x, c2) < 1)) --c2;
+    if ((x.nb_local + c2 - 1) / c2 > sd::kLocalKeysMax) break;
+    x.C = c2;
+  }
+  if (!fits())
     return fail(SD_ERR_CAPACITY, "batch*kv_heads (%lld) needs %zu bytes of scratch; the limit is %zu",
-                (long long)BH, 256 + ep_bytes + slot_bytes(x.R), kNoAllocScratch);
+                (long long)BH, 256 + ep_bytes + slot_bytes(x.C, x.R), kNoAllocScratch);
   void* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc != SD_OK) return rc;
   uint8_t* sb = static_cast<uint8_t*>(scratch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  SD_CUDA(cudaMemsetAsync(sb, 0, 256 + ep_bytes + slot_bytes(x.R), st));
+  SD_CUDA(cudaMemsetAsync(sb, 0, 256 + ep_bytes + slot_bytes(x.C, x.R), st));
 
   x.k_data = arrays->k_data; x.v_data = arrays->v_data;
   x.k_scales = arrays->k_scales; x.k_biases = arrays->k_biases;
