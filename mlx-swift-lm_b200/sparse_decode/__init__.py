@@ -420,3 +420,5 @@ def sharded_decode(index, q, k_new=None, v_new=None, scale=None, group=None, sel
 
 
 from .cache import SparseKVCache, attention_with_cache_update  # noqa: E402,F401
+from .persist import (load_prompt_cache, make_prompt_cache, maybe_quantize_kv_cache,  # noqa: E402,F401
+                      save_prompt_cache)

@@ -141,13 +141,15 @@ class SparseKVCache:
 
     @property
     def meta_state(self):
+        """[step, offset, groupSize, bits] as QuantizedKVCache's metaState
+        (KVCache.swift:900-944), then blockSize, topK and nQueryHeads."""
         return [str(self.step), str(self.offset), str(self.group_size), str(self.bits), str(self.block_size),
-                str(self.top_k)]
+                str(self.top_k), str(self.n_q_heads)]
 
     @meta_state.setter
     def meta_state(self, values):
-        if len(values) != 6:
-            raise ValueError("SparseKVCache metaState must have exactly 6 values")
+        if len(values) != 7:
+            raise ValueError("SparseKVCache metaState must have exactly 7 values")
         if self.index is not None:
             self.index.set_offset(int(values[1]))
 
