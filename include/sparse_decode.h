@@ -194,6 +194,17 @@ int32_t sd_comm_destroy(sd_comm* comm);
 int32_t sd_shard_decode(sd_index* idx, sd_comm* comm, const void* q, const void* k_new, const void* v_new,
                         float scale, void* out, int32_t* sel_out, sd_stream stream);
 
+/* Attention sinks for the decodes of this index (sd_decode, sd_shard_decode,
+ * sd_shard_merge): `sinks` is a device array of n_q_heads fp32 logits, in the
+ * units of scale * q.k, that join every head's softmax denominator without
+ * contributing a value -- out = sum_t e^(s_t) v_t / (sum_t e^(s_t) + e^(sink)),
+ * as MLXFast.scaledDotProductAttention(..., sinks:) computes it for the
+ * reference's sink-attention models (Libraries/MLXLLM/Models/GPTOSS.swift:
+ * 228-261, MiMoV2Flash.swift:14-56). NULL turns them off. The array must stay
+ * valid while decodes that use it run. The reference rejects sinks with a
+ * quantized cache; this library applies them to every cache format. */
+int32_t sd_set_sinks(sd_index* idx, const float* sinks);
+
 /* Decode launches of this index may overlap the previous kernel on the
  * stream (programmatic dependent launch): the decode kernel starts its
  * prologue -- barrier setup and the first loads of this index's summary keys

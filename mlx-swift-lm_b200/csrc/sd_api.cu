@@ -117,6 +117,7 @@ struct sd_index {
   bool racc_undo;       // the other buffer holds the sums before the last single-token append
   int* d_err;
   int overlap;          // launch decodes with programmatic stream serialization
+  const float* sinks;   // [Hq] attention-sink logits (device), or null
   CUtensorMap tmK, tmV;
   sd::KernelSet ks;
   bool attrs_set;
@@ -291,6 +292,7 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
     p.racc_rebuild = x->racc_valid ? 0 : 1;
   }
   p.R = x->R;
+  p.sinks = x->sinks;
   p.gslot = x->gslot;
   p.gep = x->gep;
   const bool other_before = note_stream(st, x);
@@ -641,7 +643,10 @@ int32_t sd_shard_merge(sd_index* x, const float* all_ml, const float* all_o, voi
   if (!x || !all_ml || !all_o || !out) return fail(SD_ERR_INVALID_ARG, "NULL argument");
   const sd_config& c = x->cfg;
   int P = c.shard_count, BQ = c.batch * c.n_q_heads, D = c.head_dim;
-  void* args[6] = {&P, &BQ, &D, const_cast<float**>(&all_ml), const_cast<float**>(&all_o), &out};
+  int Hq = c.n_q_heads;
+  const float* sinks = x->sinks;
+  void* args[8] = {&P, &BQ, &D, const_cast<float**>(&all_ml), const_cast<float**>(&all_o), &out,
+                   const_cast<float**>(&sinks), &Hq};
   SD_CUDA(cudaLaunchKernel(x->ks.merge, dim3(unsigned(BQ)), dim3(128), args, 0, static_cast<cudaStream_t>(stream)));
   return SD_OK;
 }
@@ -829,6 +834,12 @@ int32_t sd_shard_decode(sd_index* x, sd_comm* m, const void* q, const void* k_ne
     if (k_new) appended_one(x);
   }
   return rc;
+}
+
+int32_t sd_set_sinks(sd_index* x, const float* sinks) {
+  if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
+  x->sinks = sinks;
+  return SD_OK;
 }
 
 int32_t sd_set_launch_overlap(sd_index* x, int32_t enable) {

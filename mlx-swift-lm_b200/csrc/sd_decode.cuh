@@ -977,7 +977,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     const int g = idx / D, d = idx % D;
     const size_t bq = size_t(b) * p.Hq + size_t(h) * G + g;
     if (p.mode == MODE_FUSED) {
-      static_cast<E*>(p.out)[bq * D + d] = Elt<E>::from_f32(Ls > 0.0f ? O / Ls : 0.0f);
+      static_cast<E*>(p.out)[bq * D + d] = Elt<E>::from_f32(normalise_out(O, Ls, M, p.sinks, int(bq % p.Hq)));
     } else if (peer) {
       // this shard's record of (group, slice) -- [2G (m, l)][slice of o] as
       // message words -- into every shard's exchange area
@@ -1078,7 +1078,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
         }
       }
       const size_t bq = size_t(b) * p.Hq + size_t(h) * G + g;
-      static_cast<E*>(p.out)[bq * D + d] = Elt<E>::from_f32(Ls > 0.0f ? O / Ls : 0.0f);
+      static_cast<E*>(p.out)[bq * D + d] = Elt<E>::from_f32(normalise_out(O, Ls, M, p.sinks, int(bq % p.Hq)));
     }
     __syncthreads();
     if (tid == 0) {
@@ -1096,7 +1096,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
 // LSE merge of P shard partials (rank order) into the output [B, Hq, D].
 template <typename E>
 __global__ void merge_kernel(int P, int BQ, int D, const float* __restrict__ ml, const float* __restrict__ o,
-                             E* __restrict__ out) {
+                             E* __restrict__ out, const float* __restrict__ sinks, int Hq) {
   const int i = blockIdx.x;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float M = -INFINITY;
@@ -1109,7 +1109,7 @@ __global__ void merge_kernel(int P, int BQ, int D, const float* __restrict__ ml,
         O += o[(size_t(r) * BQ + i) * D + d] * f;
       }
     }
-    out[size_t(i) * D + d] = Elt<E>::from_f32(Ls > 0.0f ? O / Ls : 0.0f);
+    out[size_t(i) * D + d] = Elt<E>::from_f32(normalise_out(O, Ls, M, sinks, i % Hq));
   }
 }
 

@@ -371,6 +371,15 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Softmax normalisation of a merged (m, l, o) in the exp2 domain, with an
+// optional attention sink: a per-head logit that joins the denominator and
+// contributes no value (out = o / (l + 2^(sink*log2e - m))).
+__device__ __forceinline__ float normalise_out(float O, float Ls, float M, const float* sinks, int head) {
+  if (!(Ls > 0.0f)) return 0.0f;
+  if (sinks) Ls += exp2f(__fmaf_rn(sinks[head], 1.4426950408889634f, -M));
+  return O / Ls;
+}
+
 // Split cluster barrier: arrive early, wait right before the first access to
 // a peer's shared memory (every CTA of the cluster has started by then).
 __device__ __forceinline__ void cluster_arrive_relaxed() {

@@ -8,7 +8,7 @@ struct KernelSet {
   const void* decode;   // decode_kernel<E, BITS, D, G>(DecodeParams, CUtensorMap, CUtensorMap)
   const void* append;   // append_kernel<E, BITS, D>(AppendParams)
   const void* summary;  // summary_kernel<E, BITS, D>(SummaryParams)
-  const void* merge;    // merge_kernel<E>(int, int, int, const float*, const float*, E*)
+  const void* merge;    // merge_kernel<E>(int, int, int, const float*, const float*, E*, const float*, int)
 };
 
 // e: 0 = fp32, 1 = fp16, 2 = bf16; b: code bits (0 = dense). Null members

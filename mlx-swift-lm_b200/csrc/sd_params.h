@@ -42,6 +42,7 @@ struct DecodeParams {
   const float* racc_in;   // [BH, D] fp32 sum of the recent block's rows before this step
   float* racc_out;        // [BH, D] the same sum after the appended row
   int racc_rebuild;       // 1: racc_in is not valid; sum the recent block's rows from the cache
+  const float* sinks;     // [Hq] attention-sink logits (same units as scale * q.k), or null
   // Peer mode: every shard's exchange area mapped into this process (own at
   // [pr]). Area layout, identical on every shard, all message words (32-bit
   // payload | epoch << 32): [P][BH][K][2] candidate keys (hi, lo) at x_cand,

@@ -38,7 +38,7 @@ EXPORTED = ["sd_abi_version", "sd_status_string", "sd_last_error", "sd_index_cre
             "sd_set_offset", "sd_rebuild_summaries", "sd_decode", "sd_shard_candidates", "sd_shard_attend",
             "sd_shard_merge", "sd_check_device", "sd_set_launch_overlap", "sd_decode_noalloc", "sd_comm_create",
             "sd_comm_handle", "sd_comm_open", "sd_comm_open_local", "sd_comm_set_wait_limit", "sd_comm_destroy",
-            "sd_shard_decode"]
+            "sd_shard_decode", "sd_set_sinks"]
 COMM_HANDLE_BYTES = 128
 
 
@@ -106,6 +106,7 @@ def lib() -> ctypes.CDLL:
             "sd_comm_set_wait_limit": ([vp, i64], i32),
             "sd_comm_destroy": ([vp], i32),
             "sd_shard_decode": ([vp, vp, vp, vp, vp, f32, vp, vp, vp], i32),
+            "sd_set_sinks": ([vp, vp], i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -157,6 +158,7 @@ class SparseIndex:
                  capacity: int, dtype: str = "bf16", kv_bits: int = 0, group_size: int = 64, shard_rank: int = 0,
                  shard_count: int = 1, cluster_size: int = 0, _handle: Optional[int] = None):
         self.dtype = dtype
+        self._sinks = None
         self.cfg = SDConfig(batch, n_q_heads, n_kv_heads, head_dim, block_size, top_k, capacity, DTYPES[dtype],
                             kv_bits, group_size if kv_bits else 0, shard_rank, shard_count, cluster_size)
         if _handle is None:
@@ -261,9 +263,12 @@ class SparseIndex:
         h = ctypes.c_void_p()
         _check(lib().sd_index_copy(self._h, ctypes.byref(h), _stream(stream)))
         c = self.cfg
-        return SparseIndex(c.batch, c.n_q_heads, c.n_kv_heads, c.head_dim, c.block_size, c.top_k, c.capacity,
-                           self.dtype, c.kv_bits, c.group_size or 64, c.shard_rank, c.shard_count, c.cluster_size,
-                           _handle=h.value)
+        dup = SparseIndex(c.batch, c.n_q_heads, c.n_kv_heads, c.head_dim, c.block_size, c.top_k, c.capacity,
+                          self.dtype, c.kv_bits, c.group_size or 64, c.shard_rank, c.shard_count, c.cluster_size,
+                          _handle=h.value)
+        if self._sinks is not None:
+            dup.set_sinks(self._sinks)
+        return dup
 
     # -- decode ----------------------------------------------------------------
     def decode(self, q, k_new=None, v_new=None, scale: Optional[float] = None, out=None, sel_out=None,
@@ -305,6 +310,18 @@ class SparseIndex:
         _check(lib().sd_shard_decode(self._h, comm._h, _ptr(q), _ptr(k_new), _ptr(v_new), scale, _ptr(out),
                                      _ptr(sel_out), _stream(stream)))
         return out
+
+    def set_sinks(self, sinks) -> None:
+        """Attention-sink logits [n_q_heads] (fp32 CUDA tensor, kept alive by
+        the index) joining every head's softmax denominator; None turns them
+        off. See sd_set_sinks."""
+        if sinks is not None:
+            import torch
+            sinks = sinks.detach().to(torch.float32).contiguous()
+            if sinks.numel() != self.Hq or not sinks.is_cuda:
+                raise ValueError(f"sinks must be a CUDA tensor of {self.Hq} values")
+        self._sinks = sinks
+        _check(lib().sd_set_sinks(self._h, _ptr(sinks)))
 
     def set_launch_overlap(self, enable: bool = True) -> None:
         """Let decode launches overlap the previous kernel on the stream

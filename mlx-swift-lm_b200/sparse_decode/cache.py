@@ -204,7 +204,7 @@ class SparseKVCache:
             self._grow(self.offset + L)
         self.index.append(keys.contiguous(), values.contiguous())
 
-    def _decode(self, queries, keys, values, scale: float):
+    def _decode(self, queries, keys, values, scale: float, sinks=None):
         """One fused launch: append the token, score, select, attend."""
         import torch
         B, Hkv, L, D = keys.shape
@@ -213,13 +213,17 @@ class SparseKVCache:
             self._create(B, Hkv, D, dtype, 1)
         elif self.offset + 1 > self.index.capacity:
             self._grow(self.offset + 1)
+        if sinks is not getattr(self.index, "_sinks_src", None):
+            self.index.set_sinks(sinks)
+            self.index._sinks_src = sinks
         q = queries[:, :, 0, :].contiguous()
         out = self.index.decode(q, keys[:, :, 0, :].contiguous(), values[:, :, 0, :].contiguous(), scale)
         return out[:, :, None, :]
 
 
-def _dense_attention(queries, keys, values, scale: float, mask):
-    """Dense SDPA over cached tokens (prefill only; not the retrieval path)."""
+def _dense_attention(queries, keys, values, scale: float, mask, sinks=None):
+    """Dense SDPA over cached tokens (prefill only; not the retrieval path).
+    `sinks` [Hq]: per-head logits joining the softmax denominator."""
     import torch
     import torch.nn.functional as F
     B, Hq, L, D = queries.shape
@@ -228,11 +232,17 @@ def _dense_attention(queries, keys, values, scale: float, mask):
     v = values.repeat_interleave(G, dim=1).to(queries.dtype)
     if isinstance(mask, str) and mask == "causal":
         T = k.shape[2]
-        m = torch.arange(T - L, T, device=queries.device)[:, None] >= torch.arange(T, device=queries.device)[None]
-        return F.scaled_dot_product_attention(queries, k, v, attn_mask=m, scale=scale)
-    if mask is not None:
+        mask = torch.arange(T - L, T, device=queries.device)[:, None] >= torch.arange(T, device=queries.device)[None]
+    elif mask is not None:
         mask = mask.to(queries.device)
-    return F.scaled_dot_product_attention(queries, k, v, attn_mask=mask, scale=scale)
+    if sinks is None:
+        return F.scaled_dot_product_attention(queries, k, v, attn_mask=mask, scale=scale)
+    s = torch.einsum("bhld,bhtd->bhlt", queries.float(), k.float()) * scale
+    if mask is not None:
+        s = s.masked_fill(~mask, float("-inf")) if mask.dtype == torch.bool else s + mask
+    sink = sinks.float().view(1, Hq, 1, 1).expand(B, Hq, L, 1)
+    p = torch.softmax(torch.cat([s, sink], dim=-1), dim=-1)[..., :-1]
+    return torch.einsum("bhlt,bhtd->bhld", p, v.float()).to(queries.dtype)
 
 
 def _dequantize(wq, scales, biases, bits: int):
@@ -247,19 +257,21 @@ def _dequantize(wq, scales, biases, bits: int):
     return torch.addcmul(b, s, codes).to(scales.dtype)
 
 
-def attention_with_cache_update(queries, keys, values, cache, scale: float, mask=None):
-    """Router (AttentionUtils.swift:37-77). queries [B, Hq, L, D]; keys/values
-    [B, Hkv, L, D]. Returns [B, Hq, L, D]."""
+def attention_with_cache_update(queries, keys, values, cache, scale: float, mask=None, sinks=None):
+    """Router (AttentionUtils.swift:37-77; with `sinks`, the sink variant of
+    MiMoV2Flash.swift:14-56). queries [B, Hq, L, D]; keys/values
+    [B, Hkv, L, D]; sinks [Hq] or None. Returns [B, Hq, L, D]."""
     if cache is None:
-        return _dense_attention(queries, keys, values, scale, mask)
+        return _dense_attention(queries, keys, values, scale, mask, sinks)
     if isinstance(cache, SparseKVCache):
         if queries.shape[2] == 1:
-            return cache._decode(queries, keys, values, scale)
+            out = cache._decode(queries, keys, values, scale, sinks)
+            return out
         if cache.bits:
             (kq, ks, kb), (vq, vs, vb) = cache.update_quantized(keys, values)
             k = _dequantize(kq, ks, kb, cache.bits)
             v = _dequantize(vq, vs, vb, cache.bits)
         else:
             k, v = cache.update(keys, values)
-        return _dense_attention(queries, k, v, scale, mask)
+        return _dense_attention(queries, k, v, scale, mask, sinks)
     raise TypeError(f"unsupported cache type {type(cache).__name__}")
