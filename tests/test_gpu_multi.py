@@ -76,7 +76,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_sharded_decode_across_gpus(cuda, world):
     import torch
     import torch.multiprocessing as mp
