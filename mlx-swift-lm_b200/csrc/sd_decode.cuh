@@ -805,7 +805,18 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     }
     const int N = P * K;
     const bool small = N <= kAllKeysMax && K <= 128;
-    // small unions are staged in shared memory, clear of the runs and the pick list
+    // When every shard's list is the sorted output of its block top-K (each
+    // shard holds more than K candidates and at most kAllKeysMax), the
+    // union's top-K is a merge of P sorted runs: the lists land straight in
+    // runs of L = 64/128 keys and only the merge levels run. Otherwise the
+    // union is staged in shared memory and fully sorted.
+    const int RL = K <= 64 ? 64 : 128;
+    bool presorted = small && P * RL <= kAllKeysMax;
+    for (int r = 0; r < P; ++r) {
+      const int nl = ncand > r ? (ncand - r + P - 1) / P : 0;
+      presorted = presorted && nl > K && nl <= kAllKeysMax;
+    }
+    unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 32 * 1024);
     unsigned long long* uk = reinterpret_cast<unsigned long long*>(sm + L.ring + 80 * 1024);
     const unsigned long long* ck = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_cand);
     auto cword = [&](int i) { return ck + ((size_t(i / K) * BHn + bh) * K + (i % K)) * 2; };
@@ -815,17 +826,25 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       const uint32_t hi = ld_msg(cword(i), epoch, p.peer_wait_ns, p.err, &ok);
       const uint32_t lo = ld_msg(cword(i) + 1, epoch, p.peer_wait_ns, p.err, &ok);
       const unsigned long long x = (static_cast<unsigned long long>(hi) << 32) | lo;
-      if (small) uk[i] = x;
+      if (presorted) runs[(i / K) * RL + (i % K)] = x;
+      else if (small) uk[i] = x;
       nz += x != 0ull;
     }
+    if (presorted)
+      for (int i = tid; i < P * (RL - K); i += kThreads) runs[(i / (RL - K)) * RL + K + (i % (RL - K))] = 0ull;
     const int U = __syncthreads_count(nz > 0) > 0 ? N : 0;  // any candidate at all
     if (U == 0) {
       kk = 0;
     } else if (small) {
-      unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 32 * 1024);
-      auto ukey = [&](int i) -> unsigned long long { return uk[i]; };
-      if (K <= 64) block_topk<2>(ukey, N, runs, lane, warp, kThreads / 32);
-      else block_topk<4>(ukey, N, runs, lane, warp, kThreads / 32);
+      auto sync_all = [] { __syncthreads(); };
+      if (presorted) {
+        if (RL == 64) block_merge_runs<2>(runs, P, lane, warp, kThreads / 32, sync_all);
+        else block_merge_runs<4>(runs, P, lane, warp, kThreads / 32, sync_all);
+      } else {
+        auto ukey = [&](int i) -> unsigned long long { return uk[i]; };
+        if (K <= 64) block_topk<2>(ukey, N, runs, lane, warp, kThreads / 32);
+        else block_topk<4>(ukey, N, runs, lane, warp, kThreads / 32);
+      }
       kk = __syncthreads_count(tid < K && runs[tid] != 0ull);
       for (int i = tid; i < kk; i += kThreads) {
         const unsigned long long x = runs[i];
@@ -872,9 +891,20 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     own = sel;
     nown = n_sel;
   } else {
+    // one warp keeps the order with ballots
+    if (warp == 0) {
+      int base = 0;
+      for (int i0 = 0; i0 < n_sel; i0 += 32) {
+        const int i = i0 + lane;
+        const bool mine = i < n_sel && sel[i] % P == pr;
+        const unsigned bal = __ballot_sync(0xffffffffu, mine);
+        if (mine) own[base + __popc(bal & ((1u << lane) - 1u))] = sel[i];
+        base += __popc(bal);
+      }
+      if (lane == 0) scratch[126] = base;
+    }
     __syncthreads();
-    nown = cta_compact(n_sel, [&](int i) { return sel[i] % P == pr; }, [&](int pos, int i) { own[pos] = sel[i]; },
-                       scratch);
+    nown = scratch[126];
   }
 
   // ---------------- phase 3: attention over the staged tiles ----------------

@@ -543,6 +543,32 @@ __device__ __forceinline__ void block_topk(KeyF keyf, int n, unsigned long long*
   }
 }
 
+// The top L keys of nrun runs that are each already sorted descending
+// (runs[r*L .. r*L + L), 0-padded): the merge levels of block_topk alone.
+template <int RR, class Sync>
+__device__ __forceinline__ void block_merge_runs(unsigned long long* runs, int nrun, int lane, int warp, int nwarps,
+                                                 Sync sync) {
+  constexpr int L = 32 * RR;
+  for (int s = 1; s < nrun; s <<= 1) {
+    for (int a = warp * 2 * s; a < nrun; a += nwarps * 2 * s) {
+      const int b = a + s;
+      if (b < nrun) {
+        unsigned long long v[RR];
+#pragma unroll
+        for (int r = 0; r < RR; ++r) {
+          const int e = r * 32 + lane;
+          const unsigned long long x = runs[a * L + e], y = runs[b * L + (L - 1 - e)];
+          v[r] = x > y ? x : y;
+        }
+        warp_bitonic_merge_desc<RR>(v, lane);
+#pragma unroll
+        for (int r = 0; r < RR; ++r) runs[a * L + r * 32 + lane] = v[r];
+      }
+    }
+    sync();
+  }
+}
+
 // Number of entries of a descending list of distinct keys that exceed x.
 __device__ __forceinline__ int count_greater(const unsigned long long* a, int len, unsigned long long x) {
   int lo = 0, hi = len;
