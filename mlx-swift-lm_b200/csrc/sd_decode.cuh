@@ -976,20 +976,29 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
 
   // ---------------- phase 4: merge ----------------
   float* cpart = reinterpret_cast<float*>(sm + L.cpart);  // [G] m, [G] l, [G][D] o
-  for (int idx = tid; idx < G * D; idx += kThreads) {
-    const int g = idx / D, d = idx % D;
+  // the warps' rescale factors first (one exp2 per warp and head), then o
+  float* wf = reinterpret_cast<float*>(sm + L.recv);  // [kConsumerWarps][G]
+  if (tid < kConsumerWarps * G) {
+    const int w = tid / G, g = tid % G;
     float M = -INFINITY;
-    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mw[w * WSTRIDE + g]);
-    float Ls = 0.0f, O = 0.0f;
-    if (M != -INFINITY) {
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float f = exp2f(mw[w * WSTRIDE + g] - M);
-        Ls += mw[w * WSTRIDE + G + g] * f;
-        O += mw[w * WSTRIDE + 2 * G + g * D + d] * f;
-      }
-    }
-    if (d == 0) { cpart[g] = M; cpart[G + g] = Ls; }
-    cpart[2 * G + g * D + d] = O;
+#pragma unroll
+    for (int w2 = 0; w2 < kConsumerWarps; ++w2) M = fmaxf(M, mw[w2 * WSTRIDE + g]);
+    wf[tid] = M == -INFINITY ? 0.0f : exp2f(mw[w * WSTRIDE + g] - M);
+    if (w == 0) cpart[g] = M;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float Ls = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) Ls += mw[w * WSTRIDE + G + tid] * wf[w * G + tid];
+    cpart[G + tid] = Ls;
+  }
+  for (int idx = tid; idx < G * D; idx += kThreads) {
+    const int g = idx / D;
+    float O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) O += mw[w * WSTRIDE + 2 * G + idx] * wf[w * G + g];
+    cpart[2 * G + idx] = O;
   }
   // The group's Q = C*R CTAs merge through L2: output elements are cut into Q
   // slices, CTA q owns slice q. Every CTA sends each owner a record -- the
