@@ -59,11 +59,30 @@ __device__ __forceinline__ int cta_compact(int n, Pred pred, Emit emit, int* scr
   return total;
 }
 
+// A consumer waits on a stage's full barrier for a reused stage only once the
+// producer has issued its unit: several warps share a stage (the stage count
+// need not be a multiple of the warp count), and a warp waiting two phases
+// ahead of a stage would see the phase of the same parity before it as
+// complete. (A stage's first use waits for phase 0 of a fresh barrier, which
+// cannot be mistaken.)
+__device__ __forceinline__ bool wait_issued(const volatile int* issued, int i, int* err) {
+  if (*issued > i) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (*issued > i) return true;
+    if ((it & 255u) == 0u && globaltimer() - t0 > kWaitLimitNs) {
+      if (err) atomicOr(err, kErrTimeout);
+      return false;
+    }
+  }
+}
+
 // What a consumer warp needs to walk its tiles.
 struct TileWalk {
   uint8_t* ring;       // stage s at ring + s * stage bytes
   uint64_t* full;
   uint64_t* empty;
+  const volatile int* issued;  // units the producer has issued so far
   const int* own;      // selected blocks of this shard, recent last
   int u0, nmine, tpb;  // this CTA's units [u0, u0 + nmine), tiles per block
   float* mw;           // per-warp partial slots (m[G], l[G], o[G][D])
@@ -91,7 +110,8 @@ __device__ __forceinline__ void consume_tiles_fma(const DecodeParams& p, const T
   const uint32_t qf_a = smem_u32(qf);
   for (int i = warp; i < tw.nmine; i += kConsumerWarps) {
     const int s = i % F::kStages;
-    if (mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
+    if ((i < F::kStages || wait_issued(tw.issued, i, p.err)) &&
+        mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
       const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
       const int nv = min(TS, T - (j * S + tile * TS));
       uint8_t* stage = tw.ring + s * F::kStageBytes;
@@ -308,7 +328,8 @@ __device__ __forceinline__ void consume_tiles_mma(const DecodeParams& p, const T
   const int mq = lane >> 3, r8 = lane & 7;
   for (int i = warp; i < tw.nmine; i += kConsumerWarps) {
     const int s = i % F::kStages;
-    if (mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
+    if ((i < F::kStages || wait_issued(tw.issued, i, p.err)) &&
+        mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
       const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
       const int nv = min(TS, T - (j * S + tile * TS));
       const uint32_t kb = smem_u32(tw.ring + s * F::kStageBytes);
@@ -444,6 +465,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   if (tid == 0) {
     for (int s = 0; s < F::kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     fence_mbar_init();
+    scratch[124] = 0;  // units issued by the producer
   }
   if (warp == kConsumerWarps && lane == 0 && p.mode != MODE_CANDIDATES) {
     prefetch_tensormap(&tmK);
@@ -915,7 +937,8 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   const int nmine = u1 - u0;
   constexpr int WSTRIDE = G * D + 2 * G;
   float* mw = reinterpret_cast<float*>(sm + L.ring);  // per-warp partials, once every stage is consumed
-  const TileWalk tw{sm + L.ring, full, empty, own, u0, nmine, tpb, mw};
+  volatile int* issued = scratch + 124;  // zeroed in phase 0
+  const TileWalk tw{sm + L.ring, full, empty, issued, own, u0, nmine, tpb, mw};
   constexpr bool kMma = BITS == 0 && sizeof(E) == 2;
 
   if (warp == kConsumerWarps) {
@@ -940,6 +963,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
         bulk_load(sb + 3 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_biases) + so, F::kSbTileBytes,
                   full + s);
       }
+      *issued = i + 1;
     };
     if (lane == 0) {
       fence_proxy_async_shared();

@@ -68,6 +68,20 @@ def test_c1_full_size_layer(cuda):
     _check(w, c, res, idx)
 
 
+@pytest.mark.parametrize("bits", [0, 8, 4])
+def test_many_tiles_per_cta(cuda, bits):
+    """One CTA per group (cluster 1, no replicas) walks hundreds of 32-token
+    tiles through the TMA ring, so every stage is reused many times by
+    different consumer warps (the shape of config 3, where 128 groups fill the
+    GPU with one CTA each)."""
+    w = Workload("many", B=2, Hq=8, Hkv=2, D=128, T=64 * 140 + 33, S=64, K=128, dtype="bf16", bits=bits,
+                 needles=5)
+    c, idx, res = run_decode(w, seed=31, cluster=1)
+    assert idx.cluster_size == 1 and idx.replicas == 1
+    assert res["err"] == 0
+    _check(w, c, res, idx)
+
+
 @pytest.mark.parametrize("cluster", [1, 2, 4, 8, 16])
 def test_cluster_sizes_agree(cuda, cluster):
     w = CONFIGS["c1"].with_(T=6000, K=20)
