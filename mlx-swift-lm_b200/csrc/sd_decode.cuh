@@ -412,6 +412,227 @@ __device__ __forceinline__ void consume_tiles_mma(const DecodeParams& p, const T
   }
 }
 
+// Tensor-core consumer for 4/8-bit K/V with 16-bit scales (fp16 or bf16
+// caches). The codes stay exact: ldmatrix brings a 16-byte piece of a row
+// into registers, a byte permute puts each code in the mantissa of the fp16
+// 1024 + c, and a packed subtraction leaves c itself. q . k over one
+// quantization group of 64 dims is then one fp16 product per k-step
+// (q.c, accumulated in fp32) and k's affine form is applied per token in
+// fp32: q.k = s * (q.c) + b * sum(q). The order of the dims inside a k-step
+// is permuted on both operands alike (a dot product does not care), which is
+// what lets one 32-bit register of ldmatrix output feed the mma directly. For
+// p.v the codes of two consecutive tokens are paired the same way from
+// ldmatrix.trans, and p' = p * s_v (per token and group, as hi + lo fp16) is
+// the A operand; the bias part sum_t p * b_v is accumulated on the side. q is scaled by 2^-eq
+// so that its fp16 form cannot overflow; eq is undone on the product.
+__device__ __forceinline__ uint32_t code_pair_u8(uint32_t r, uint32_t sel) {
+  const uint32_t h = __byte_perm(r, 0x6464u, sel);  // fp16 1024 + c in each half
+  uint32_t out;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(out) : "r"(h), "r"(0x64006400u));
+  return out;
+}
+__device__ __forceinline__ uint32_t code_pair_u4(uint32_t r, int j) {
+  const uint32_t h = ((r >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+  uint32_t out;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(out) : "r"(h), "r"(0x64006400u));
+  return out;
+}
+
+template <typename E, int BITS, int D, int G>
+__device__ __forceinline__ void consume_tiles_qmma(const DecodeParams& p, const TileWalk& tw, const E* qg,
+                                                   const float* qs, int warp, int lane) {
+  using F = Fmt<2, BITS, D>;
+  constexpr int TS = kTileTokens, NT = TS / 8, NG = F::kGroups, NCH = F::kNChunk;
+  constexpr int KSTEPS = D / 16;                 // 16-dim k-steps of q.k
+  constexpr int CPG = 64 / F::kEpc;              // 16-byte chunks per quantization group
+  constexpr int NPC = BITS == 8 ? 2 : 4;         // p.v n-tiles (8 dims each) per chunk
+  constexpr int ND = NCH * NPC;                  // p.v n-tiles = D / 8
+  static_assert(ND == D / 8, "n-tile count");
+  const int g = lane >> 2, tq = lane & 3;
+  const int S = p.S, T = p.T;
+  // q of head g (rows 8..15 are zero), scaled by 2^-eq, in the permuted order
+  float qmax = 0.0f;
+  for (int i = lane; i < G * D; i += 32) qmax = fmaxf(qmax, fabsf(Elt<E>::to_f32(qg[i])));
+  qmax = warp_max(qmax);
+  const int eq = qmax > 16384.0f ? (ilogbf(qmax) - 13) : 0;
+  const float qscale = ldexpf(1.0f, -eq);
+  auto qv = [&](int d) { return g < G ? Elt<E>::to_f32(qg[g * D + d]) * qscale : 0.0f; };
+  uint32_t qa0[KSTEPS], qa2[KSTEPS];
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks) {
+    if constexpr (BITS == 8) {
+      const int d = 16 * ks + 4 * tq;  // chunk ks: dims 4tq..4tq+3 of this lane's register
+      qa0[ks] = pack2<__half>(qv(d), qv(d + 1));
+      qa2[ks] = pack2<__half>(qv(d + 2), qv(d + 3));
+    } else {
+      const int c = ks >> 1, h = ks & 1;  // chunk c holds 32 dims; k-step h of it
+      const int d = 32 * c + 8 * tq + 2 * h;
+      qa0[ks] = pack2<__half>(qv(d), qv(d + 4));
+      qa2[ks] = pack2<__half>(qv(d + 1), qv(d + 5));
+    }
+  }
+  const float qfac = ldexpf(p.scale_log2, eq);  // undoes 2^-eq and applies scale * log2(e)
+  float m_run = -INFINITY, l_run = 0.0f, ob[NG];
+  float o[ND][4];
+#pragma unroll
+  for (int r = 0; r < NG; ++r) ob[r] = 0.0f;
+#pragma unroll
+  for (int nd = 0; nd < ND; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.0f;
+  const int mq = lane >> 3, r8 = lane & 7;
+  auto chunk_addr = [&](uint32_t base, int row, int c) {
+    const int bx = c / F::kCpb, cc = c % F::kCpb;
+    return base + bx * TS * F::kBoxBytes + swz(uint32_t(row * F::kBoxBytes + cc * 16), F::kCpb);
+  };
+  for (int i = warp; i < tw.nmine; i += kConsumerWarps) {
+    const int s = i % F::kStages;
+    if ((i < F::kStages || wait_issued(tw.issued, i, p.err)) &&
+        mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
+      const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
+      const int nv = min(TS, T - (j * S + tile * TS));
+      uint8_t* stage = tw.ring + s * F::kStageBytes;
+      const uint32_t kb = smem_u32(stage);
+      const uint32_t vb = kb + F::kKvTileBytes;
+      const E* ksc = reinterpret_cast<const E*>(stage + 2 * F::kKvTileBytes);
+      const E* kbi = ksc + TS * NG;
+      const E* vsc = ksc + 2 * TS * NG;
+      const E* vbi = ksc + 3 * TS * NG;
+      // --- q.c per group: lane m of the x4 load supplies row r8 of token block mq ---
+      float acc[NG][NT][4];
+#pragma unroll
+      for (int r = 0; r < NG; ++r)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[r][nt][0] = acc[r][nt][1] = acc[r][nt][2] = acc[r][nt][3] = 0.0f;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        uint32_t rk[4];
+        ldsm_x4(chunk_addr(kb, 8 * mq + r8, c), rk[0], rk[1], rk[2], rk[3]);
+        const int grp = c / CPG;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          if constexpr (BITS == 8) {
+            mma16816<__half>(acc[grp][nt], qa0[c], qa2[c], code_pair_u8(rk[nt], 0x4140u),
+                             code_pair_u8(rk[nt], 0x4342u));
+          } else {
+            mma16816<__half>(acc[grp][nt], qa0[2 * c], qa2[2 * c], code_pair_u4(rk[nt], 0),
+                             code_pair_u4(rk[nt], 1));
+            mma16816<__half>(acc[grp][nt], qa0[2 * c + 1], qa2[2 * c + 1], code_pair_u4(rk[nt], 2),
+                             code_pair_u4(rk[nt], 3));
+          }
+        }
+      }
+      // scores (log2 units) of head g for tokens 8nt + 2tq + e
+      float sc[NT][2];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = 8 * nt + 2 * tq + e;
+          float v = 0.0f;
+          if (t < nv && g < G) {
+#pragma unroll
+            for (int r = 0; r < NG; ++r) {
+              const float s_ = Elt<E>::to_f32(ksc[t * NG + r]), b_ = Elt<E>::to_f32(kbi[t * NG + r]);
+              v = fmaf(s_, acc[r][nt][e] * qfac, fmaf(b_, qs[g * NG + r], v));
+            }
+          }
+          sc[nt][e] = t < nv ? v : -INFINITY;
+          mx = fmaxf(mx, sc[nt][e]);
+        }
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m_run, mx);
+      const float alpha = exp2f(m_run - mn);
+      float rs = 0.0f, bsum[NG];
+#pragma unroll
+      for (int r = 0; r < NG; ++r) bsum[r] = 0.0f;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = 8 * nt + 2 * tq + e;
+          sc[nt][e] = t < nv ? exp2f(sc[nt][e] - mn) : 0.0f;
+          rs += sc[nt][e];
+          if (t < nv) {
+#pragma unroll
+            for (int r = 0; r < NG; ++r) bsum[r] = fmaf(sc[nt][e], Elt<E>::to_f32(vbi[t * NG + r]), bsum[r]);
+          }
+        }
+      }
+      rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+      rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+#pragma unroll
+      for (int r = 0; r < NG; ++r) {
+        bsum[r] += __shfl_xor_sync(0xffffffffu, bsum[r], 1);
+        bsum[r] += __shfl_xor_sync(0xffffffffu, bsum[r], 2);
+        ob[r] = ob[r] * alpha + bsum[r];
+      }
+      l_run = l_run * alpha + rs;
+      m_run = mn;
+#pragma unroll
+      for (int nd = 0; nd < ND; ++nd) { o[nd][0] *= alpha; o[nd][1] *= alpha; }
+      // --- p'.c: k-steps of 16 tokens; A = p * s_v per group (fp16) ---
+#pragma unroll
+      for (int kt = 0; kt < NT / 2; ++kt) {
+        // p' as hi + lo fp16 pairs (~22 significant bits): the code and bias
+        // parts of p.v can nearly cancel, so p' must not lose more than fp32
+        // would in the sum
+        uint32_t pa0[NG], pa2[NG], pl0[NG], pl2[NG];
+#pragma unroll
+        for (int r = 0; r < NG; ++r) {
+          const int t0 = 16 * kt + 2 * tq, t2 = t0 + 8;
+          auto sv = [&](int t) { return t < nv ? Elt<E>::to_f32(vsc[t * NG + r]) : 0.0f; };
+          split2<__half>(sc[2 * kt][0] * sv(t0), sc[2 * kt][1] * sv(t0 + 1), pa0[r], pl0[r]);
+          split2<__half>(sc[2 * kt + 1][0] * sv(t2), sc[2 * kt + 1][1] * sv(t2 + 1), pa2[r], pl2[r]);
+        }
+#pragma unroll
+        for (int c = 0; c < NCH; c += 2) {
+          // matrices: tokens 16kt + {0..7, 8..15} of chunks c and c + 1
+          uint32_t rv[4];
+          ldsm_x4_t(chunk_addr(vb, 16 * kt + 8 * (mq & 1) + r8, c + (mq >> 1)), rv[0], rv[1], rv[2], rv[3]);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int cc = c + h, grp = cc / CPG;
+            const uint32_t lo = rv[2 * h], hi = rv[2 * h + 1];
+#pragma unroll
+            for (int jn = 0; jn < NPC; ++jn) {
+              uint32_t b0, b1;
+              if constexpr (BITS == 8) {
+                const uint32_t sel = jn == 0 ? 0x4240u : 0x4341u;
+                b0 = code_pair_u8(lo, sel);
+                b1 = code_pair_u8(hi, sel);
+              } else {
+                b0 = code_pair_u4(lo, jn);
+                b1 = code_pair_u4(hi, jn);
+              }
+              mma16816<__half>(o[cc * NPC + jn], pa0[grp], pa2[grp], b0, b1);
+              mma16816<__half>(o[cc * NPC + jn], pl0[grp], pl2[grp], b0, b1);
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tw.empty + s);
+  }
+  named_barrier(1, kConsumerWarps * 32);  // all consumers are done with the ring
+  float* w = tw.mw + warp * (G * D + 2 * G);
+  if (g < G) {
+    if (tq == 0) { w[g] = m_run; w[G + g] = l_run; }
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd) {
+      const int c = nd / NPC, jn = nd % NPC;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int n = 2 * tq + e;  // column of the n-tile
+        const int d = BITS == 8 ? 16 * c + 2 * n + jn : 32 * c + 4 * n + jn;
+        w[2 * G + g * D + d] = o[nd][e] + ob[d / 64];
+      }
+    }
+  }
+}
+
 template <typename E, int BITS, int D, int G>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap tmK,
@@ -940,6 +1161,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   volatile int* issued = scratch + 124;  // zeroed in phase 0
   const TileWalk tw{sm + L.ring, full, empty, issued, own, u0, nmine, tpb, mw};
   constexpr bool kMma = BITS == 0 && sizeof(E) == 2;
+  constexpr bool kQMma = BITS != 0 && sizeof(E) == 2;
 
   if (warp == kConsumerWarps) {
     auto issue = [&](int i) {
@@ -992,6 +1214,8 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     __syncwarp();
   } else if constexpr (kMma) {
     consume_tiles_mma<E, D, G>(p, tw, qg, warp, lane);
+  } else if constexpr (kQMma) {
+    consume_tiles_qmma<E, BITS, D, G>(p, tw, qg, qs, warp, lane);
   } else {
     float* ps = reinterpret_cast<float*>(sm + L.ps + warp * align_up(TS * G * NG * 4, 16));
     consume_tiles_fma<E, BITS, D, G>(p, tw, qf, qs, ps, warp, lane);

@@ -28,6 +28,10 @@ SMALL = [
     CONFIGS["c2q4"].with_(B=2, T=8192),                                # 4-bit
     Workload("q8_f16_d64", B=1, Hq=4, Hkv=2, D=64, T=2000, S=64, K=10, dtype="f16", bits=8, needles=3),
     Workload("q4_f32_d64", B=1, Hq=8, Hkv=2, D=64, T=1500, S=32, K=12, dtype="f32", bits=4, needles=3),
+    Workload("q4_bf16_d64_g8", B=1, Hq=16, Hkv=2, D=64, T=2500, S=64, K=9, dtype="bf16", bits=4, needles=3),
+    Workload("q8_f16_d128_g1", B=2, Hq=2, Hkv=2, D=128, T=2100, S=32, K=14, dtype="f16", bits=8, needles=2),
+    Workload("q4_f16_d128_g2", B=1, Hq=4, Hkv=2, D=128, T=3100, S=128, K=5, dtype="f16", bits=4, needles=2),
+    Workload("q8_bf16_d64_g8", B=1, Hq=16, Hkv=2, D=64, T=1700, S=64, K=7, dtype="bf16", bits=8, needles=2),
 ]
 
 
