@@ -184,23 +184,6 @@ __device__ __forceinline__ void st_msg_gpu(unsigned long long* p, uint32_t paylo
   const unsigned long long v = (static_cast<unsigned long long>(epoch) << 32) | payload;
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_msg_gpu(const unsigned long long* p, uint32_t epoch, uint64_t limit_ns,
-                                               int* err, bool* ok) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  if (uint32_t(v >> 32) == epoch) return uint32_t(v);
-  if (!*ok) return 0u;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t it = 1;; ++it) {
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    if (uint32_t(v >> 32) == epoch) return uint32_t(v);
-    if ((it & 15u) == 0u && globaltimer() - t0 > limit_ns) {
-      if (err) atomicOr(err, kErrTimeout);
-      *ok = false;
-      return 0u;
-    }
-  }
-}
 // The payload of a message word once it carries `epoch`; on expiry of
 // limit_ns the error word is set, *ok cleared, and 0 returned.
 __device__ __forceinline__ uint32_t ld_msg(const unsigned long long* p, uint32_t epoch, uint64_t limit_ns, int* err,
@@ -394,21 +377,8 @@ __device__ __forceinline__ uint32_t map_rank(uint32_t local_smem_addr, uint32_t 
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
 __device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_cluster_v2(uint32_t addr, uint32_t a, uint32_t b) {
-  asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
-}
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
-  return v;
 }
 
 // ---------------------------------------------------------------------------
