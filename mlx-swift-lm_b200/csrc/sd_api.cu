@@ -166,18 +166,25 @@ int32_t validate(const sd_config* c) {
   return SD_OK;
 }
 
+// The K or V arena as a 3-D byte tensor (column box, row, box index): a row
+// of row_bytes is cut into boxes of min(row_bytes, 128) bytes, the widest the
+// swizzle allows, and one copy moves a whole tile of kTileTokens rows with all
+// its boxes, landing as [box][row][box bytes] in shared memory. One TMA
+// operation per tile rather than one per box: the SM's TMA unit spends a fixed
+// time on each operation, which dominates copies of a few KB.
 int32_t encode_map(CUtensorMap* map, void* base, int row_bytes, int64_t rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(SD_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const int box_bytes = std::min(row_bytes, 128);
+  const int nbox = row_bytes / box_bytes;
   CUtensorMapSwizzle sw = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                           : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                             : CU_TENSOR_MAP_SWIZZLE_32B;
-  cuuint64_t dims[2] = {cuuint64_t(row_bytes), cuuint64_t(rows)};
-  cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
-  cuuint32_t box[2] = {cuuint32_t(box_bytes), cuuint32_t(sd::kTileTokens)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr,
+  cuuint64_t dims[3] = {cuuint64_t(box_bytes), cuuint64_t(rows), cuuint64_t(nbox)};
+  cuuint64_t strides[2] = {cuuint64_t(row_bytes), cuuint64_t(box_bytes)};
+  cuuint32_t box[3] = {cuuint32_t(box_bytes), cuuint32_t(sd::kTileTokens), cuuint32_t(nbox)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));

@@ -1170,11 +1170,8 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       const int row = bh * p.cap_local + (j / P) * S + tile * TS;
       uint8_t* st = sm + L.ring + s * F::kStageBytes;
       mbar_arrive_expect_tx(full + s, 2 * F::kKvTileBytes + 4 * F::kSbTileBytes);
-#pragma unroll
-      for (int bx = 0; bx < F::kNBox; ++bx) {
-        tma_load_2d(st + bx * TS * F::kBoxBytes, &tmK, bx * F::kBoxBytes, row, full + s);
-        tma_load_2d(st + F::kKvTileBytes + bx * TS * F::kBoxBytes, &tmV, bx * F::kBoxBytes, row, full + s);
-      }
+      tma_load_3d(st, &tmK, 0, row, 0, full + s);  // all column boxes of the tile
+      tma_load_3d(st + F::kKvTileBytes, &tmV, 0, row, 0, full + s);
       if constexpr (BITS != 0) {
         const size_t so = size_t(row) * NG * sizeof(E);
         uint8_t* sb = st + 2 * F::kKvTileBytes;
