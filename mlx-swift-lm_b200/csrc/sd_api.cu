@@ -118,7 +118,8 @@ struct sd_index {
   int* d_err;
   int overlap;          // launch decodes with programmatic stream serialization
   const float* sinks;   // [Hq] attention-sink logits (device), or null
-  CUtensorMap tmK, tmV;
+  CUtensorMap tmK, tmV, tmS;
+  int sb_fused;         // tmS covers the four scale/bias arrays
   sd::KernelSet ks;
   bool attrs_set;
 };
@@ -189,6 +190,23 @@ int32_t encode_map(CUtensorMap* map, void* base, int row_bytes, int64_t rows) {
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
   return SD_OK;
+}
+
+// The four scale/bias arrays of a quantized index (k_scales, k_biases,
+// v_scales, v_biases, each `bytes` long, one every `stride` bytes) as a 2-D
+// byte tensor: one copy moves the tile's four pieces of tile_bytes, stacked
+// as the kernel's stage expects. The byte coordinate is a signed 32-bit
+// number, so arrays of 2 GiB or more keep the 1-D bulk copies.
+bool encode_sb_map(CUtensorMap* map, void* base, size_t stride, size_t bytes, int tile_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || stride % 16 != 0 || bytes >= (size_t(1) << 31) || tile_bytes % 16 != 0 || tile_bytes > 256) return false;
+  cuuint64_t dims[2] = {cuuint64_t(bytes), 4};
+  cuuint64_t strides[1] = {cuuint64_t(stride)};
+  cuuint32_t box[2] = {cuuint32_t(tile_bytes), 4};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Number of clusters of size C the device can hold at once (0 = not launchable).
@@ -333,7 +351,8 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = overlap ? 2 : 1;
-  void* args[3] = {&p, &x->tmK, &x->tmV};
+  p.sb_fused = x->sb_fused;
+  void* args[4] = {&p, &x->tmK, &x->tmV, &x->tmS};
   SD_CUDA(cudaLaunchKernelExC(&cfg, x->ks.decode, args));
   return SD_OK;
 }
@@ -473,6 +492,11 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
     delete x;
     return fail(SD_ERR_CUDA, "cudaMemset failed: %s", cudaGetErrorString(e));
   }
+  // One copy per tile for the four scale/bias pieces: the arena keeps the
+  // four arrays sb bytes apart.
+  std::memset(&x->tmS, 0, sizeof(x->tmS));
+  x->sb_fused = c.kv_bits && encode_sb_map(&x->tmS, x->k_scales, sb, size_t(BH) * x->cap_local * x->groups * x->esize,
+                                           sd::kTileTokens * x->groups * x->esize) ? 1 : 0;
   rc = encode_map(&x->tmK, x->k_data, x->row_bytes, BH * x->cap_local);
   if (rc == SD_OK) rc = encode_map(&x->tmV, x->v_data, x->row_bytes, BH * x->cap_local);
   if (rc != SD_OK) {
@@ -1028,7 +1052,8 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   attr[0].val.clusterDim.z = 1;
   lc.attrs = attr;
   lc.numAttrs = 1;
-  void* args[3] = {&p, &x.tmK, &x.tmV};
+  p.sb_fused = 0;  // the caller's arrays: four 1-D bulk scale/bias copies
+  void* args[4] = {&p, &x.tmK, &x.tmV, &x.tmS};
   SD_CUDA(cudaLaunchKernelExC(&lc, x.ks.decode, args));
   return SD_OK;
 }

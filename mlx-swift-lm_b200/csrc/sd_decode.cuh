@@ -636,7 +636,7 @@ __device__ __forceinline__ void consume_tiles_qmma(const DecodeParams& p, const 
 template <typename E, int BITS, int D, int G>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap tmK,
-              const __grid_constant__ CUtensorMap tmV) {
+              const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmS) {
   using F = Fmt<int(sizeof(E)), BITS, D>;
   constexpr int NG = F::kGroups;
   constexpr int TS = kTileTokens;
@@ -691,6 +691,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   if (warp == kConsumerWarps && lane == 0 && p.mode != MODE_CANDIDATES) {
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
+    if (BITS != 0 && p.sb_fused) prefetch_tensormap(&tmS);
   }
   const bool owner_recent = ((NB - 1) % P) == pr;
   const bool appending = p.k_new != nullptr && p.mode != MODE_ATTEND && owner_recent && crank == C - 1;
@@ -1170,17 +1171,23 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       const int row = bh * p.cap_local + (j / P) * S + tile * TS;
       uint8_t* st = sm + L.ring + s * F::kStageBytes;
       mbar_arrive_expect_tx(full + s, 2 * F::kKvTileBytes + 4 * F::kSbTileBytes);
-      tma_load_3d(st, &tmK, 0, row, 0, full + s);  // all column boxes of the tile
+      // the tile's K and V, all column boxes of each (two copies: one 4-D copy
+      // of both measured slower at a few tiles per CTA)
+      tma_load_3d(st, &tmK, 0, row, 0, full + s);
       tma_load_3d(st + F::kKvTileBytes, &tmV, 0, row, 0, full + s);
       if constexpr (BITS != 0) {
         const size_t so = size_t(row) * NG * sizeof(E);
         uint8_t* sb = st + 2 * F::kKvTileBytes;
-        bulk_load(sb, static_cast<const uint8_t*>(p.k_scales) + so, F::kSbTileBytes, full + s);
-        bulk_load(sb + F::kSbTileBytes, static_cast<const uint8_t*>(p.k_biases) + so, F::kSbTileBytes, full + s);
-        bulk_load(sb + 2 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_scales) + so, F::kSbTileBytes,
-                  full + s);
-        bulk_load(sb + 3 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_biases) + so, F::kSbTileBytes,
-                  full + s);
+        if (p.sb_fused) {
+          tma_load_2d(sb, &tmS, int32_t(so), 0, full + s);  // so < 2^31 whenever the map is used
+        } else {
+          bulk_load(sb, static_cast<const uint8_t*>(p.k_scales) + so, F::kSbTileBytes, full + s);
+          bulk_load(sb + F::kSbTileBytes, static_cast<const uint8_t*>(p.k_biases) + so, F::kSbTileBytes, full + s);
+          bulk_load(sb + 2 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_scales) + so, F::kSbTileBytes,
+                    full + s);
+          bulk_load(sb + 3 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_biases) + so, F::kSbTileBytes,
+                    full + s);
+        }
       }
       *issued = i + 1;
     };

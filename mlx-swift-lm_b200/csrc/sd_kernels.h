@@ -5,7 +5,7 @@
 namespace sd {
 
 struct KernelSet {
-  const void* decode;   // decode_kernel<E, BITS, D, G>(DecodeParams, CUtensorMap, CUtensorMap)
+  const void* decode;   // decode_kernel<E, BITS, D, G>(DecodeParams, CUtensorMap x3)
   const void* append;   // append_kernel<E, BITS, D>(AppendParams)
   const void* summary;  // summary_kernel<E, BITS, D>(SummaryParams)
   const void* merge;    // merge_kernel<E>(int, int, int, const float*, const float*, E*, const float*, int)

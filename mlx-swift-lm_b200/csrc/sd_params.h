@@ -52,6 +52,10 @@ struct DecodeParams {
   uint8_t* peer[8];
   int64_t x_cand, x_part, x_ctl;  // byte offsets inside an area
   uint64_t peer_wait_ns;                   // bound of every wait for another shard
+  // 1: the scale/bias tensor map covers the four arrays (k_scales, k_biases,
+  // v_scales, v_biases at one fixed stride), one copy per tile. 0: four 1-D
+  // bulk copies.
+  int sb_fused;
 };
 
 struct AppendParams {
