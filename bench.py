@@ -14,8 +14,9 @@ same context. Inputs are synthetic (seeded) and device-resident; a step
 moves 36 x 18.1 MB, larger than the 126 MB L2, so no flush is needed.
 
 N > 1 (torchrun, one process per GPU): the same workload sequence-sharded
-(block j on rank j % N), with NCCL all-gathers of the top-K candidates and
-of the (m, l, o) partials: strong scaling of the per-layer latency.
+(block j on rank j % N) through the fused peer-memory step -- one launch per
+layer and GPU that exchanges the top-K candidates and the (m, l, o) partials
+with the other shards over NVLink: strong scaling of the per-layer latency.
 
 `--impl reference` times the CPU restatement of the path (oracle/, all host
 threads) on the same workload: the reference's own implementation (Swift +
@@ -174,8 +175,8 @@ def run_reference(args, w, rank: int, world: int) -> None:
     v = statistics.median(vals)
     line = {"metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(v * w.layers / 1000, 4), "higher_is_better": False,
-            "scaling": "strong", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded; 16 needle blocks)",
-            "impl": "reference",
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": w.dtype,
+            "data": "synthetic (seeded N(0,1) Q/K/V, planted needle blocks)", "impl": "reference",
             "config": {"workload": w.name, "batch": w.B, "q_heads": w.Hq, "kv_heads": w.Hkv, "head_dim": w.D,
                        "context": w.T, "block": w.S, "top_k": w.K, "layers_per_step": w.layers},
             "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port",
