@@ -17,7 +17,10 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def test_noalloc_decode_matches_sd_decode_twice(cuda):
+@pytest.mark.parametrize("bits", [0, 8])
+def test_noalloc_decode_matches_sd_decode_twice(cuda, bits):
+    """bits 8: the caller's scale/bias arrays reach the kernel as four 1-D
+    bulk copies per tile (the index's own arena uses one tiled copy)."""
     import torch
 
     import sparse_decode as sd
@@ -26,10 +29,11 @@ def test_noalloc_decode_matches_sd_decode_twice(cuda):
     from _util import assert_close, host_case
     from gpu_cases import to_dev, to_host
 
-    w = CONFIGS["c1"].with_(T=8192)  # 8 (batch, kv-head) groups: several replicas, so the scratch holds partials
+    # 8 (batch, kv-head) groups: several replicas, so the scratch holds partials
+    w = CONFIGS["c1"].with_(T=8192, bits=bits)
     c = host_case(w, seed=77)
     B, Hkv, T, D = w.B, w.Hkv, w.T, w.D
-    idx = sd.SparseIndex(B, w.Hq, Hkv, D, w.S, w.K, T, w.dtype)
+    idx = sd.SparseIndex(B, w.Hq, Hkv, D, w.S, w.K, T, w.dtype, w.bits)
     assert idx.replicas > 1
     k = to_dev(c["ks"].reshape(B, Hkv, T, D), w.dtype)
     v = to_dev(c["vs"].reshape(B, Hkv, T, D), w.dtype)
