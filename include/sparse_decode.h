@@ -230,9 +230,13 @@ int32_t sd_check_device(sd_index* idx, int32_t* flags, sd_stream stream);
  * scales/biases for 4/8-bit caches, summaries, cap_local, nb_local; e.g.
  * arrays filled earlier through an index, or by the caller's own code), the
  * number of tokens `offset`, queries, output and an optional sel_out, and the
- * call decodes one token (no append) like sd_decode. device_flags (nullable,
+ * call decodes one token (no append) like sd_decode. device_flags (required:
  * a caller-owned device int, zeroed by the caller) receives the same error
- * bits as sd_check_device reports.
+ * bits as sd_check_device reports; there is no other place where a call's
+ * device errors could be read. Alignment: k_data, v_data, summaries and the
+ * four scale/bias arrays 16 bytes (the kernel reads them with 16-byte loads
+ * and bulk copies), q and device_flags 4 bytes, out 2 bytes; a misaligned
+ * pointer is rejected with SD_ERR_INVALID_ARG before anything is launched.
  * The kernel's scratch (the message words through which the CTAs of a
  * (batch, kv-head) group merge their partial results, and the groups' epochs)
  * lives in a fixed array of SD_NOALLOC_SCRATCH_BYTES of device memory inside

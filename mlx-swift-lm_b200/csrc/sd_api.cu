@@ -122,6 +122,7 @@ struct sd_index {
   int sb_fused;         // tmS covers the four scale/bias arrays
   sd::KernelSet ks;
   bool attrs_set;
+  unsigned long long* dbg;  // phase-timing build: stamp buffer of the decode launches
 };
 
 // Exchange area of one shard for the fused sharded step (sd_shard_decode);
@@ -352,6 +353,7 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   cfg.attrs = attr;
   cfg.numAttrs = overlap ? 2 : 1;
   p.sb_fused = x->sb_fused;
+  p.dbg = x->dbg;
   void* args[4] = {&p, &x->tmK, &x->tmV, &x->tmS};
   SD_CUDA(cudaLaunchKernelExC(&cfg, x->ks.decode, args));
   return SD_OK;
@@ -879,6 +881,23 @@ int32_t sd_set_launch_overlap(sd_index* x, int32_t enable) {
   return SD_OK;
 }
 
+#ifdef SD_PHASE_TIMING
+// Phase-timing build only: decode launches of this index write their phase
+// stamps ([grid.y][grid.x][8] u64, see SD_STAMP_* in sd_device.cuh) to buf;
+// NULL turns the stamps off.
+int32_t sd_debug_set_phase_buffer(sd_index* x, void* buf) {
+  if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
+  x->dbg = static_cast<unsigned long long*>(buf);
+  return SD_OK;
+}
+int32_t sd_debug_grid(const sd_index* x, int32_t* grid_x, int32_t* grid_y) {
+  if (!x || !grid_x || !grid_y) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  *grid_x = x->C * x->R;
+  *grid_y = x->cfg.batch * x->cfg.n_kv_heads;
+  return SD_OK;
+}
+#endif
+
 int32_t sd_check_device(sd_index* x, int32_t* flags, sd_stream stream) {
   if (!x || !flags) return fail(SD_ERR_INVALID_ARG, "NULL argument");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -897,8 +916,9 @@ int32_t sd_check_device(sd_index* x, int32_t* flags, sd_stream stream) {
 //
 // For callers that own every byte of device memory themselves: the keys,
 // values, scales, biases and summary keys are their arrays, and the decode
-// kernel's replica partials, arrival counters and error word live in one
-// fixed array of device memory that this file defines. Every GPU that loads
+// kernel's scratch -- the message words through which the CTAs of a group
+// merge their partials, and the groups' epochs -- lives in one fixed array of
+// device memory that this file defines. Every GPU that loads
 // the library holds that array until the process exits; all calls on a GPU
 // share it and it keeps the last call's contents, so calls that overlap on
 // the GPU (two streams, or two host threads) race with each other.
@@ -938,6 +958,9 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   int32_t rc = validate(cfg);
   if (rc != SD_OK) return rc;
   if (!arrays || !q || !out) return fail(SD_ERR_INVALID_ARG, "NULL argument");
+  // The error bits have nowhere else to go: the scratch array is cleared by
+  // the next call before the caller could read it.
+  if (!device_flags) return fail(SD_ERR_INVALID_ARG, "device_flags is required (the kernel's error bits go there)");
   const sd_config& c = *cfg;
   if (c.shard_count != 1) return fail(SD_ERR_STATE, "sd_decode_noalloc serves single-shard caches only");
   if (!std::isfinite(scale)) return fail(SD_ERR_INVALID_ARG, "scale must be finite");
@@ -945,6 +968,16 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
     return fail(SD_ERR_INVALID_ARG, "k_data, v_data and summaries are required");
   if (c.kv_bits && (!arrays->k_scales || !arrays->k_biases || !arrays->v_scales || !arrays->v_biases))
     return fail(SD_ERR_INVALID_ARG, "quantized caches need scales and biases");
+  // The kernel reads these arrays with 16-byte loads and bulk copies, the
+  // queries with 4-byte loads; a misaligned pointer would fault on the GPU.
+  auto mis = [](const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) != 0; };
+  if (mis(arrays->k_data, 16) || mis(arrays->v_data, 16) || mis(arrays->summaries, 16))
+    return fail(SD_ERR_INVALID_ARG, "k_data, v_data and summaries must be 16-byte aligned");
+  if (c.kv_bits && (mis(arrays->k_scales, 16) || mis(arrays->k_biases, 16) || mis(arrays->v_scales, 16) ||
+                    mis(arrays->v_biases, 16)))
+    return fail(SD_ERR_INVALID_ARG, "scales and biases must be 16-byte aligned");
+  if (mis(q, 4) || mis(out, 2) || mis(sel_out, 4) || mis(device_flags, 4))
+    return fail(SD_ERR_INVALID_ARG, "q must be 4-byte, out 2-byte, sel_out and device_flags 4-byte aligned");
   if (arrays->cap_local < 1 || arrays->cap_local % c.block_size != 0 || offset < 1 || offset > arrays->cap_local)
     return fail(SD_ERR_SHAPE, "offset %lld / cap_local %lld do not describe a cache", (long long)offset,
                 (long long)arrays->cap_local);
@@ -1032,7 +1065,7 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   p.summ = x.summ;
   p.out = out;
   p.sel_out = sel_out;
-  p.err = device_flags ? device_flags : reinterpret_cast<int*>(sb);
+  p.err = device_flags;
   p.R = x.R;
   p.gep = reinterpret_cast<uint32_t*>(sb + 256);
   p.gslot = x.C * x.R > 1 ? reinterpret_cast<unsigned long long*>(sb + 256 + ep_bytes) : nullptr;

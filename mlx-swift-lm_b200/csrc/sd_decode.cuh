@@ -645,6 +645,8 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   const Layout L = make_layout(D, G, NG);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  SD_STAMP_T(p, 0);
+  SD_STAMP_C(p, 1);
   const int C = p.C, R = p.R;
   const int crank = C > 1 ? int(cluster_ctarank()) : 0;
   const int rep = blockIdx.x / C;  // replica cluster of this CTA
@@ -770,6 +772,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   }
 
   // ---------------- phase 1: block scores ----------------
+  SD_STAMP_C(p, 2);
   // (the producer warp appends the new token meanwhile)
   if (C > 1) cluster_wait();
   if (warp == kConsumerWarps && appending) {
@@ -851,6 +854,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   }
 
   // ---------------- phase 2: selection ----------------
+  SD_STAMP_C(p, 3);
   int kk;  // blocks chosen by top-K
   if (whole) {
     if (C > 1) cluster_sync();  // every peer's pushed keys have landed
@@ -1123,6 +1127,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   }
 
   // Selected blocks (in selection order), then the recent block.
+  SD_STAMP_C(p, 4);
   for (int i = tid; i < kk; i += kThreads) sel[i] = int(pick[i].y);
   if (tid == 0) sel[kk] = NB - 1;
   __syncthreads();
@@ -1225,6 +1230,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     consume_tiles_fma<E, BITS, D, G>(p, tw, qf, qs, ps, warp, lane);
   }
   __syncthreads();  // warp partials are in mw
+  SD_STAMP_C(p, 5);
 
   // ---------------- phase 4: merge ----------------
   float* cpart = reinterpret_cast<float*>(sm + L.cpart);  // [G] m, [G] l, [G][D] o
@@ -1333,6 +1339,8 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     __syncthreads();
     if (qrank == 0 && tid == 0) p.gep[bh] = gep;
   }
+  SD_STAMP_C(p, 6);
+  SD_STAMP_T(p, 7);
   if (!peer) return;
 
   // ---------------- peer mode: merge the shards ----------------
@@ -1381,6 +1389,8 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
         ctl[0] = epoch;
       }
     }
+    SD_STAMP_C(p, 6);
+    SD_STAMP_T(p, 7);
   }
 }
 

@@ -126,6 +126,32 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// Phase stamps of the decode kernel, compiled only into the phase-timing
+// build (-DSD_PHASE_TIMING): thread 0 of every CTA writes 8 u64 per CTA to
+// DecodeParams::dbg -- [0] %globaltimer at entry, [1..6] clock64 at entry,
+// scoring start, scoring end, selection end, attention end, merge end, [7]
+// %globaltimer at exit. The product build has no stamps.
+#ifdef SD_PHASE_TIMING
+__device__ __forceinline__ unsigned long long clock_u64() {
+  unsigned long long c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
+#define SD_STAMP_T(p, k)                                                                   \
+  do {                                                                                     \
+    if (threadIdx.x == 0 && (p).dbg)                                                        \
+      (p).dbg[(size_t(blockIdx.y) * gridDim.x + blockIdx.x) * 8 + (k)] = ::sd::globaltimer(); \
+  } while (0)
+#define SD_STAMP_C(p, k)                                                                   \
+  do {                                                                                     \
+    if (threadIdx.x == 0 && (p).dbg)                                                        \
+      (p).dbg[(size_t(blockIdx.y) * gridDim.x + blockIdx.x) * 8 + (k)] = ::sd::clock_u64();   \
+  } while (0)
+#else
+#define SD_STAMP_T(p, k) do { } while (0)
+#define SD_STAMP_C(p, k) do { } while (0)
+#endif
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }

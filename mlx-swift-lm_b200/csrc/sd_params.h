@@ -56,6 +56,7 @@ struct DecodeParams {
   // v_scales, v_biases at one fixed stride), one copy per tile. 0: four 1-D
   // bulk copies.
   int sb_fused;
+  unsigned long long* dbg;  // phase-timing build only: [grid.y][grid.x][8] stamps, or null
 };
 
 struct AppendParams {

@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 from pathlib import Path
 from typing import Optional
 
@@ -71,10 +72,11 @@ def lib() -> ctypes.CDLL:
     """Load libsparse_decode.so; raises when it has not been built."""
     global _lib
     if _lib is None:
-        if not LIB_PATH.exists():
-            raise RuntimeError(f"{LIB_PATH} is missing: build it with __graft_entry__.build() "
+        path = Path(os.environ.get("SPARSE_DECODE_LIB", str(LIB_PATH)))
+        if not path.exists():
+            raise RuntimeError(f"{path} is missing: build it with __graft_entry__.build() "
                                "(the CUDA path has no fallback)")
-        L = ctypes.CDLL(str(LIB_PATH))
+        L = ctypes.CDLL(str(path))
         vp, i32, i64, f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
         pp = ctypes.POINTER(ctypes.c_void_p)
         sig = {

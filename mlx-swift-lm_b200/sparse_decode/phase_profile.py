@@ -1,0 +1,147 @@
+"""Per-phase timing of the decode kernel inside CUDA-graph replays.
+
+Uses the phase-timing build of the library (libsparse_decode_phases.so, see
+sparse_decode.build): thread 0 of every CTA stamps %globaltimer at entry and
+exit and clock64 at the phase boundaries (entry, scoring start, scoring end,
+selection end, attention end, merge end). This module builds `layers`
+independent single-layer indexes of a workload exactly as bench.py does,
+captures one decode step of all of them in a CUDA graph, replays it, and
+reports per phase the median and maximum over CTAs (microseconds, clock64
+cycles converted with each CTA's own cycles-per-ns), plus the layer cadence
+seen by %globaltimer.
+
+    python -m sparse_decode.phase_profile --config c1 --layers 36
+
+Run from mlx-swift-lm_b200/ (or with it on sys.path); needs a GPU.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import sys
+from pathlib import Path
+
+PHASES = ["prologue", "score", "select", "attend", "merge"]
+
+
+def _load_phase_lib():
+    from . import build as b
+    path = b.LIB_PHASES if b.LIB_PHASES.exists() else b.build(phase_timing=True)
+    os.environ["SPARSE_DECODE_LIB"] = str(path)
+    import sparse_decode
+    if sparse_decode._lib is not None and not hasattr(sparse_decode._lib, "sd_debug_set_phase_buffer"):
+        raise RuntimeError("the product library is already loaded in this process")
+    L = sparse_decode.lib()
+    L.sd_debug_set_phase_buffer.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    L.sd_debug_set_phase_buffer.restype = ctypes.c_int32
+    L.sd_debug_grid.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]
+    L.sd_debug_grid.restype = ctypes.c_int32
+    return L
+
+
+def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True) -> dict:
+    import torch
+
+    L = _load_phase_lib()
+    from sparse_decode import SparseIndex, _check
+    from sparse_decode.synth import CONFIGS, algorithmic_bytes, make_case_torch
+
+    w = CONFIGS[config].with_(layers=layers)
+    scale = 1.0 / math.sqrt(w.D)
+    items = []
+    for l in range(layers):
+        case = make_case_torch(w, seed=1000 + l)
+        idx = SparseIndex(w.B, w.Hq, w.Hkv, w.D, w.S, w.K, w.T, w.dtype, w.bits)
+        k, v = case["k"], case["v"]
+        idx.append(k[:, :, : w.T - 1].contiguous(), v[:, :, : w.T - 1].contiguous())
+        idx.set_launch_overlap(overlap)
+        gx, gy = ctypes.c_int32(), ctypes.c_int32()
+        _check(L.sd_debug_grid(idx._h, ctypes.byref(gx), ctypes.byref(gy)))
+        buf = torch.zeros((gy.value, gx.value, 8), dtype=torch.int64, device="cuda")
+        _check(L.sd_debug_set_phase_buffer(idx._h, ctypes.c_void_p(buf.data_ptr())))
+        items.append({"idx": idx, "q": case["q"].contiguous(), "k": k[:, :, w.T - 1].contiguous(),
+                      "v": v[:, :, w.T - 1].contiguous(), "out": torch.empty_like(case["q"]), "buf": buf})
+        del case, k, v
+    torch.cuda.synchronize()
+    for it in items:
+        it["idx"].decode(it["q"], it["k"], it["v"], scale, out=it["out"])
+    for it in items:
+        it["idx"].trim(1)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for it in items:
+            it["idx"].decode(it["q"], it["k"], it["v"], scale, out=it["out"])
+    for it in items:
+        it["idx"].trim(1)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us_layer = e0.elapsed_time(e1) * 1000.0 / layers
+    err = sum(it["idx"].check_device() for it in items)
+
+    per_phase = {p: [] for p in PHASES}
+    per_phase_max = {p: [] for p in PHASES}
+    spans, entries, exits, skews = [], [], [], []
+    for it in items:
+        a = it["buf"].cpu().reshape(-1, 8).tolist()
+        ph = {p: [] for p in PHASES}
+        for r in a:
+            gt0, c1, c2, c3, c4, c5, c6, gt7 = r
+            ns = gt7 - gt0
+            cyc = c6 - c1
+            cpn = cyc / ns if ns > 0 else 1.965
+            for p_, (x, y) in zip(PHASES, [(c1, c2), (c2, c3), (c3, c4), (c4, c5), (c5, c6)]):
+                ph[p_].append((y - x) / cpn / 1000.0)
+        for p_ in PHASES:
+            per_phase[p_].append(statistics.median(ph[p_]))
+            per_phase_max[p_].append(max(ph[p_]))
+        t0 = min(r[0] for r in a)
+        t1 = max(r[7] for r in a)
+        entries.append(t0)
+        exits.append(t1)
+        spans.append((t1 - t0) / 1000.0)
+        skews.append((max(r[0] for r in a) - t0) / 1000.0)
+    cad = [(entries[i + 1] - entries[i]) / 1000.0 for i in range(len(entries) - 1)]
+    gaps = [(entries[i + 1] - exits[i]) / 1000.0 for i in range(len(entries) - 1)]
+    res = {
+        "config": w.name, "layers": layers, "grid": list(items[0]["buf"].shape[:2][::-1]),
+        "us_per_layer_events": round(us_layer, 3), "device_error": err,
+        "algorithmic_bytes_per_layer": algorithmic_bytes(w),
+        "phase_us_median_over_ctas": {p: round(statistics.median(per_phase[p]), 3) for p in PHASES},
+        "phase_us_max_over_ctas": {p: round(statistics.median(per_phase_max[p]), 3) for p in PHASES},
+        "layer_span_us": round(statistics.median(spans), 3),
+        "cta_start_skew_us": round(statistics.median(skews), 3),
+        "layer_cadence_us": round(statistics.median(cad), 3) if cad else None,
+        "gap_next_entry_minus_exit_us": round(statistics.median(gaps), 3) if gaps else None,
+    }
+    del graph
+    return res
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--config", default="c1")
+    ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--no-overlap", action="store_true")
+    args = ap.parse_args()
+    import torch
+    torch.cuda.set_device(0)
+    print(json.dumps(profile(args.config, args.layers, args.warmup, not args.no_overlap)), flush=True)
+
+
+if __name__ == "__main__":
+    here = Path(__file__).resolve().parent.parent
+    if str(here) not in sys.path:
+        sys.path.insert(0, str(here))
+    main()

@@ -7,9 +7,10 @@ PARITY UNPINNED: the reference snapshot holds no implementation of this path
 and no golden vectors for it, and MLX (which holds the quantization and SDPA
 arithmetic the reference calls) is not vendored. This package exposes:
 
-* `sd_oracle.cpp` (built as liboracle.so) through ctypes -- the canonical-order
-  restatement used for bit-exact selection checks, fp64 attention, and the
-  timed fp32 CPU baseline;
+* `sd_oracle.cpp` (built into liboracle.so) through ctypes -- the canonical-order
+  restatement used for bit-exact selection checks and fp64 attention;
+* `sd_cpu_baseline.cpp` (same library) -- the timed fp32 CPU implementation of
+  the whole path (thread pool, AVX2), checked against the fp64 oracle;
 * a pure-numpy twin of each stage (`np_*`), written independently, used at
   small sizes to cross-check the C++ restatement.
 
@@ -66,8 +67,10 @@ def lib() -> ctypes.CDLL:
         L.orc_topk.restype = i32
         L.orc_attend_f64.argtypes = [vp, i32, kvp, kvp, i32, i32, i32, i32, i32, vp, i32, i32, f64, i32, vp, vp, vp]
         L.orc_merge_f64.argtypes = [i32, i64, i32, vp, vp, vp, vp]
-        L.orc_decode_f32.argtypes = [vp, i32, kvp, kvp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32, vp, vp, i32]
-        L.orc_decode_f32.restype = i32
+        L.orc_base_set_threads.argtypes = [i32]
+        L.orc_base_last_threads.restype = i32
+        L.orc_base_decode.argtypes = [vp, i32, kvp, kvp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32, vp, vp]
+        L.orc_base_decode.restype = i32
         _lib = L
     return _lib
 
@@ -214,15 +217,23 @@ def merge_f64(m: np.ndarray, l_: np.ndarray, o: np.ndarray) -> np.ndarray:
 
 
 def decode_f32(q, qdtype, Kc: Cache, Vc: Cache, summ, sdtype, B, Hq, Hkv, T, S, K, scale, threads=0):
-    """Whole path in fp32 on host threads (the timed CPU baseline)."""
+    """Whole path in fp32 on host threads: the timed CPU implementation
+    (sd_cpu_baseline.cpp; threads=0 uses every hardware thread). Returns
+    (out, sel); `last_threads()` tells how many threads ran tasks."""
     D = Kc.D
     out = np.empty((B, Hq, D), NP_STORAGE[qdtype])
     n_sel = min(K, (T + S - 1) // S - 1) + 1
     sel = np.empty((B * Hkv, n_sel), np.int32)
     kv, vv = Kc.view(), Vc.view()
-    lib().orc_decode_f32(_p(np.ascontiguousarray(q)), qdtype, ctypes.byref(kv), ctypes.byref(vv), _p(summ), sdtype,
-                         summ.shape[1], B, Hq, Hkv, T, S, K, np.float32(scale), _p(out), _p(sel), threads)
+    lib().orc_base_set_threads(threads)
+    lib().orc_base_decode(_p(np.ascontiguousarray(q)), qdtype, ctypes.byref(kv), ctypes.byref(vv), _p(summ), sdtype,
+                          summ.shape[1], B, Hq, Hkv, T, S, K, np.float32(scale), _p(out), _p(sel))
     return out, sel
+
+
+def last_threads() -> int:
+    """Threads that ran at least one task in the last decode_f32 call."""
+    return int(lib().orc_base_last_threads())
 
 
 # ---------------------------------------------------------------------------

@@ -160,37 +160,41 @@ void orc_quantize(const void* x, int dtype, int64_t rows, int D, int gs, int bit
   const float n_bins = float((1 << bits) - 1);
   const int per_word = 32 / bits;
   const int words = D / per_word;
-  std::vector<float> w(gs);
-  std::vector<uint32_t> codes(D);
-  for (int64_t r = 0; r < rows; ++r) {
-    for (int g = 0; g < ng; ++g) {
-      float wmax = -INFINITY, wmin = INFINITY;
-      for (int i = 0; i < gs; ++i) {
-        w[i] = load_elt(x, dtype, r * D + g * gs + i);
-        wmax = std::max(wmax, w[i]);
-        wmin = std::min(wmin, w[i]);
+  // rows are independent: runs of 4096 rows in parallel
+  const int64_t RUN = 4096;
+  parallel_for((rows + RUN - 1) / RUN, [&](int64_t run) {
+    std::vector<float> w(gs);
+    std::vector<uint32_t> codes(D);
+    for (int64_t r = run * RUN; r < std::min(rows, (run + 1) * RUN); ++r) {
+      for (int g = 0; g < ng; ++g) {
+        float wmax = -INFINITY, wmin = INFINITY;
+        for (int i = 0; i < gs; ++i) {
+          w[i] = load_elt(x, dtype, r * D + g * gs + i);
+          wmax = std::max(wmax, w[i]);
+          wmin = std::min(wmin, w[i]);
+        }
+        float scale = std::max((wmax - wmin) / n_bins, 1e-7f);
+        const bool mask = std::fabs(wmin) > std::fabs(wmax);
+        if (!mask) scale = -scale;
+        const float edge = mask ? wmin : wmax;
+        const float q0 = std::rint(edge / scale);
+        if (q0 != 0.0f) scale = edge / q0;
+        const float bias = (q0 == 0.0f) ? 0.0f : edge;
+        for (int i = 0; i < gs; ++i) {
+          float c = std::rint((w[i] - bias) / scale);
+          c = std::min(std::max(c, 0.0f), n_bins);
+          codes[g * gs + i] = uint32_t(c);
+        }
+        store_elt(scales, dtype, r * ng + g, scale);
+        store_elt(biases, dtype, r * ng + g, bias);
       }
-      float scale = std::max((wmax - wmin) / n_bins, 1e-7f);
-      const bool mask = std::fabs(wmin) > std::fabs(wmax);
-      if (!mask) scale = -scale;
-      const float edge = mask ? wmin : wmax;
-      const float q0 = std::rint(edge / scale);
-      if (q0 != 0.0f) scale = edge / q0;
-      const float bias = (q0 == 0.0f) ? 0.0f : edge;
-      for (int i = 0; i < gs; ++i) {
-        float c = std::rint((w[i] - bias) / scale);
-        c = std::min(std::max(c, 0.0f), n_bins);
-        codes[g * gs + i] = uint32_t(c);
+      for (int k = 0; k < words; ++k) {
+        uint32_t word = 0;
+        for (int i = 0; i < per_word; ++i) word |= codes[k * per_word + i] << (bits * i);
+        wq[r * words + k] = word;
       }
-      store_elt(scales, dtype, r * ng + g, scale);
-      store_elt(biases, dtype, r * ng + g, bias);
     }
-    for (int k = 0; k < words; ++k) {
-      uint32_t word = 0;
-      for (int i = 0; i < per_word; ++i) word |= codes[k * per_word + i] << (bits * i);
-      wq[r * words + k] = word;
-    }
-  }
+  });
 }
 
 void orc_dequantize(const uint32_t* wq, const void* scales, const void* biases, int dtype,
@@ -389,67 +393,6 @@ void orc_merge_f64(int P, int64_t BQ, int D, const double* m, const double* l, c
       out[i * D + d] = L > 0 ? acc / L : 0.0;
     }
   }
-}
-
-// The whole decode path in fp32 on the host cores: scores (canonical order),
-// selection, and attention with fp32 accumulation, OpenMP over (b, kv-head).
-// This is the timed CPU baseline. out is [B, Hq, D] of qdtype; sel may be null.
-int orc_decode_f32(const void* q, int qdtype, const orc_kv_view* K, const orc_kv_view* V,
-                   const void* summ, int sdtype, int nb_stride, int B, int Hq, int Hkv, int T,
-                   int S, int k, float scale, void* out, int32_t* sel_out, int n_threads) {
-  const int G = Hq / Hkv, D = K->D;
-  const int NB = (T + S - 1) / S;
-  const int64_t BH = int64_t(B) * Hkv;
-  std::vector<float> scores(BH * NB);
-  const int n_sel = std::min(k, NB - 1) + 1;
-  std::vector<int32_t> sel(BH * n_sel);
-  const int prev = g_threads;
-  g_threads = n_threads;
-  orc_scores(q, qdtype, summ, sdtype, B, Hq, Hkv, D, NB, nb_stride, scale, scores.data());
-  orc_select(scores.data(), BH, NB, k, sel.data(), n_sel);
-  parallel_for(BH, [&](int64_t bh) {
-    const int64_t b = bh / Hkv, h = bh % Hkv;
-    std::vector<float> qv(G * D), o(G * D, 0.0f), m(G, -INFINITY), l(G, 0.0f);
-    std::vector<float> kblk(size_t(S) * D), vrow(D), s(size_t(G) * S);
-    for (int g = 0; g < G; ++g)
-      for (int d = 0; d < D; ++d) qv[g * D + d] = load_elt(q, qdtype, (b * Hq + h * G + g) * D + d) * scale;
-    for (int i = 0; i < n_sel; ++i) {
-      const int j = sel[bh * n_sel + i];
-      const int t0 = j * S, n = std::min((j + 1) * S, T) - t0;
-      for (int t = 0; t < n; ++t) load_row(K, bh, t0 + t, &kblk[size_t(t) * D]);
-      for (int g = 0; g < G; ++g) {
-        float mx = m[g];
-        for (int t = 0; t < n; ++t) {
-          float a = 0.0f;
-          for (int d = 0; d < D; ++d) a += qv[g * D + d] * kblk[size_t(t) * D + d];
-          s[size_t(g) * S + t] = a;
-          mx = std::max(mx, a);
-        }
-        const float alpha = std::exp(m[g] - mx);
-        l[g] *= alpha;
-        for (int d = 0; d < D; ++d) o[g * D + d] *= alpha;
-        for (int t = 0; t < n; ++t) {
-          const float p = std::exp(s[size_t(g) * S + t] - mx);
-          s[size_t(g) * S + t] = p;
-          l[g] += p;
-        }
-        m[g] = mx;
-      }
-      for (int t = 0; t < n; ++t) {
-        load_row(V, bh, t0 + t, vrow.data());
-        for (int g = 0; g < G; ++g) {
-          const float p = s[size_t(g) * S + t];
-          for (int d = 0; d < D; ++d) o[g * D + d] += p * vrow[d];
-        }
-      }
-    }
-    for (int g = 0; g < G; ++g)
-      for (int d = 0; d < D; ++d)
-        store_elt(out, qdtype, (b * Hq + h * G + g) * D + d, o[g * D + d] / l[g]);
-  });
-  g_threads = prev;
-  if (sel_out) std::memcpy(sel_out, sel.data(), sel.size() * sizeof(int32_t));
-  return n_sel;
 }
 
 }  // extern "C"

@@ -65,16 +65,40 @@ def assert_close(out: np.ndarray, ref: np.ndarray, dtype: str) -> None:
         assert u <= ULPS, f"element-wise error {u:.3g} ulp > {ULPS}"
 
 
+# The oracle's parallel loops use every host thread (rows and groups are
+# independent, so the results do not depend on the thread count).
+oracle.lib().orc_set_threads(0)
+
+# Above this many K elements host_case draws its inputs with torch's CPU
+# generator (many threads) instead of numpy's; same recipe, another stream.
+FAST_ELEMS = 1 << 27
+
+
+def _storage_from_torch(t, dtype: str) -> np.ndarray:
+    import torch
+    t = t.contiguous()
+    if dtype == "bf16":
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
 def host_case(w: Workload, seed: int) -> dict:
     """Synthetic case plus its oracle caches (all T rows filled), summaries,
     canonical scores, selection and fp64 outputs."""
-    from sparse_decode.synth import make_case
-    c = make_case(w, seed)
+    from sparse_decode.synth import make_case, make_case_torch
     dt = DTYPE_CODE[w.dtype]
     B, Hkv, T, D = w.B, w.Hkv, w.T, w.D
-    k = c["k"].reshape(B * Hkv, T, D)
-    v = c["v"].reshape(B * Hkv, T, D)
-    ks, vs = oracle.to_storage(k, dt), oracle.to_storage(v, dt)
+    if B * Hkv * T * D > FAST_ELEMS:
+        c = make_case_torch(w, seed, device="cpu")
+        ks = _storage_from_torch(c["k"], w.dtype).reshape(B * Hkv, T, D)
+        vs = _storage_from_torch(c["v"], w.dtype).reshape(B * Hkv, T, D)
+        c["q"] = oracle.to_f32(_storage_from_torch(c["q"], w.dtype), dt)
+        del c["k"], c["v"]
+    else:
+        c = make_case(w, seed)
+        k = c["k"].reshape(B * Hkv, T, D)
+        v = c["v"].reshape(B * Hkv, T, D)
+        ks, vs = oracle.to_storage(k, dt), oracle.to_storage(v, dt)
     if w.bits:
         kq = oracle.quantize(ks, dt, D, w.bits)
         vq = oracle.quantize(vs, dt, D, w.bits)

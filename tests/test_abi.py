@@ -136,9 +136,11 @@ def test_noalloc_validates_before_cuda(native):
     arr = sdp.SDArrays()
     q = ctypes.c_void_p(256)
 
-    def call(cfg, off, scale=0.1):
+    flags = ctypes.c_void_p(512)
+
+    def call(cfg, off, scale=0.1, fl=flags, qq=q):
         return sdp.STATUS[native.sd_decode_noalloc(None if cfg is None else ctypes.byref(cfg), ctypes.byref(arr),
-                                                   off, q, scale, q, None, None, None)]
+                                                   off, qq, scale, q, None, fl, None)]
 
     assert call(None, 1) == "SD_ERR_INVALID_ARG"
     assert call(_cfg(), 1) == "SD_ERR_INVALID_ARG"                           # k_data NULL
@@ -153,3 +155,15 @@ def test_noalloc_validates_before_cuda(native):
     assert call(_cfg(), 100) == "SD_ERR_SHAPE"
     arr.nb_local, arr.row_bytes = 64, 128
     assert call(_cfg(), 100) == "SD_ERR_SHAPE"                               # bf16 rows are 256 B
+    arr.row_bytes = 0
+    assert call(_cfg(), 100, fl=None) == "SD_ERR_INVALID_ARG"                # device_flags is required
+    # misaligned caller arrays are rejected on the host, before any launch
+    arr.summaries = 256 + 2
+    assert call(_cfg(), 100) == "SD_ERR_INVALID_ARG"
+    arr.summaries, arr.k_data = 256, 256 + 8
+    assert call(_cfg(), 100) == "SD_ERR_INVALID_ARG"
+    arr.k_data = 256
+    arr.k_scales = arr.k_biases = arr.v_scales = 1024
+    arr.v_biases = 1024 + 2
+    assert call(_cfg(kv_bits=8, group_size=64), 100) == "SD_ERR_INVALID_ARG"
+    assert call(_cfg(), 100, qq=ctypes.c_void_p(258)) == "SD_ERR_INVALID_ARG"

@@ -4,8 +4,9 @@ Some callers own all of the GPU's memory -- e.g. a serving runtime that
 reserves the device's memory pool at start-up and lends slices of it to its
 plug-ins -- and cannot let a library call cudaMalloc. For them the library
 offers one decode call that takes the caller's own cache arrays and keeps its
-scratch (replica partials and arrival counters) in a fixed device array
-compiled into the library. This file is collected last on purpose.
+scratch (the message words through which a group's CTAs merge their partial
+results, and the groups' epochs) in a fixed device array compiled into the
+library. This file is collected last on purpose.
 """
 from __future__ import annotations
 
