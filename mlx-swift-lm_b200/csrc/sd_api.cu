@@ -111,6 +111,9 @@ struct sd_index {
   void *k_data, *v_data, *k_scales, *k_biases, *v_scales, *v_biases, *summ;
   unsigned long long* gslot;  // C*R > 1: the group merge's message words
   uint32_t* gep;        // C*R > 1: epoch of each group's last merged launch
+  int mt;               // sliced selection: list length per CTA (0: the index never slices)
+  unsigned long long* clist;  // sliced selection, C*R > 1: [BH][C*R][mt][2] message words
+  unsigned long long* cfall;  // ... and [BH][C*R][top_k][2] for the full lists
   float* racc;          // 2 x [BH, D] running sums of the recent block's rows
   int racc_cur;         // buffer holding the current sums
   bool racc_valid;      // the current buffer matches the cache
@@ -231,6 +234,49 @@ int max_active_clusters(const sd_index* x, int C) {
   return n;
 }
 
+// Candidate blocks of this shard when the cache is full.
+int64_t max_local_candidates(const sd_index* x) {
+  const sd_config& c = x->cfg;
+  const int64_t ncand = x->nb_global - 1;
+  return ncand > c.shard_rank ? (ncand - c.shard_rank + c.shard_count - 1) / c.shard_count : 0;
+}
+
+// Whether a launch with nloc candidate blocks per group takes the sliced
+// selection (see decode_kernel): more than kAllKeysMax candidates, K > 128,
+// or several CTAs per group that are not one cluster.
+bool sliced_launch(const sd_index* x, int64_t nloc) {
+  return x->cfg.top_k > 128 || nloc > sd::kAllKeysMax || (x->C == 1 && x->R > 1);
+}
+
+// Length of each CTA's list in the sliced selection with Q CTAs per group:
+// about four times a CTA's share of the top-K (at least 32, at most K), so
+// that the lists hold the group's top-K unless one share is very uneven (then
+// the kernel falls back to full lists); Q * mt <= 4096 (the kernel's buffer).
+int list_len(int K, int Q) {
+  if (K <= 0) return 0;
+  int m = 4 * ((K + Q - 1) / Q);
+  m = std::max(32, (m + 31) / 32 * 32);
+  m = std::min(m, K);
+  return std::max(1, std::min(m, 4096 / Q));
+}
+
+// CTAs of a group (of Q) that own a slice of the output in the group merge:
+// about one per 128 outputs, and enough that an owner's Q records fit one
+// batch of loads (8 words per thread of the decode kernel).
+int merge_owners(int Q, int G, int D) {
+  if (Q <= 1) return 1;
+  const int GD = G * D;
+  int n = std::max(1, (GD + 127) / 128);
+  while (n < Q && int64_t(Q) * (2 * G + (GD + n - 1) / n) > 8 * sd::kThreads) ++n;
+  return std::min(n, Q);
+}
+
+// Words of one merge record: the (m, l) of every head, then an owner's slice.
+int merge_record(int Q, int G, int D) {
+  const int no = merge_owners(Q, G, D);
+  return 2 * G + (G * D + no - 1) / no;
+}
+
 int32_t setup_kernels(sd_index* x) {
   if (x->attrs_set) return SD_OK;
   SD_CUDA(cudaFuncSetAttribute(x->ks.decode, cudaFuncAttributeMaxDynamicSharedMemorySize, int(x->smem)));
@@ -259,6 +305,21 @@ int32_t choose_cluster(sd_index* x) {
     x->R = 1;
     if (max_active_clusters(x, x->C) < 1)
       return fail(SD_ERR_SHAPE, "cluster size %d cannot be scheduled with %zu bytes of shared memory", x->C, x->smem);
+    return SD_OK;
+  }
+  // Sliced selection at full capacity (K > 128 or more than kAllKeysMax
+  // candidates per group): single-CTA "clusters", Q = R CTAs per group, as
+  // many as the SMs hold at once (one CTA per SM) -- every CTA scores 1/Q of
+  // the candidates and attends 1/Q of the tiles; Q * K stays within the
+  // kernel's union buffer.
+  if (c.top_k > 128 || max_local_candidates(x) > sd::kAllKeysMax) {
+    int Q = int(std::min<int64_t>(sd::kMaxGroupCtas, std::max<int64_t>(1, n_sm / BH)));
+    if (c.top_k > 0) Q = std::min(Q, std::max(1, sd::kUnionMax / c.top_k));
+    const int mac = max_active_clusters(x, 1);
+    while (Q > 1 && mac < BH * Q) --Q;
+    if (mac < 1) return fail(SD_ERR_SHAPE, "the decode kernel cannot be scheduled with %zu bytes of shared memory", x->smem);
+    x->C = 1;
+    x->R = Q;
     return SD_OK;
   }
   // Replicas (R <= 4 clusters per group, each attending 1/R of the tiles)
@@ -318,6 +379,7 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
     p.racc_rebuild = x->racc_valid ? 0 : 1;
   }
   p.R = x->R;
+  p.nown = merge_owners(x->C * x->R, x->G, c.head_dim);
   p.sinks = x->sinks;
   p.gslot = x->gslot;
   p.gep = x->gep;
@@ -335,8 +397,16 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   }
   const int64_t ncand = p.NB - 1;
   const int64_t nloc = ncand > p.pr ? (ncand - p.pr + p.P - 1) / p.P : 0;
-  if ((nloc + x->C - 1) / x->C > sd::kLocalKeysMax)
-    return fail(SD_ERR_SHAPE, "too many blocks per CTA (%lld) for cluster size %d", (long long)((nloc + x->C - 1) / x->C), x->C);
+  p.sliced = sliced_launch(x, nloc) ? 1 : 0;
+  const int64_t chunks = p.sliced ? int64_t(x->C) * x->R : x->C;
+  if ((nloc + chunks - 1) / chunks > sd::kLocalKeysMax)
+    return fail(SD_ERR_SHAPE, "too many blocks per CTA (%lld) for %lld CTAs per group",
+                (long long)((nloc + chunks - 1) / chunks), (long long)chunks);
+  if (p.sliced && x->C * x->R > 1 && c.top_k > 0 && mode != sd::MODE_ATTEND && (!x->clist || !x->cfall))
+    return fail(SD_ERR_STATE, "index has no sliced-selection buffers");
+  p.mt = x->mt;
+  p.clist = x->clist;
+  p.cfall = x->cfall;
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(unsigned(x->C * x->R), unsigned(c.batch * c.n_kv_heads), 1);
@@ -447,8 +517,9 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
   }
   x->ks = lookup(c.dtype, c.kv_bits, c.head_dim, x->G);
   if (!x->ks.decode) {
+    const int G = x->G;
     delete x;
-    return fail(SD_ERR_SHAPE, "no kernel for dtype %d, bits %d, head_dim %d, G %d", c.dtype, c.kv_bits, c.head_dim, x->G);
+    return fail(SD_ERR_SHAPE, "no kernel for dtype %d, bits %d, head_dim %d, G %d", c.dtype, c.kv_bits, c.head_dim, G);
   }
   const sd::Layout L = sd::make_layout(c.head_dim, x->G, x->groups);
   x->smem = size_t(L.total) + 1024;
@@ -462,16 +533,21 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
   const size_t kv = align256(size_t(BH) * x->cap_local * x->row_bytes);
   const size_t sb = c.kv_bits ? align256(size_t(BH) * x->cap_local * x->groups * x->esize) : 0;
   const size_t su = align256(size_t(BH) * x->nb_local * c.head_dim * x->esize);
-  const int GD = x->G * c.head_dim;
   const int Q = x->C * x->R;
-  const size_t rp = Q > 1 ? align256(size_t(BH) * Q * Q * (2 * x->G + (GD + Q - 1) / Q) * 8) : 0;
+  const size_t rp =
+      Q > 1 ? align256(size_t(BH) * merge_owners(Q, x->G, c.head_dim) * Q * merge_record(Q, x->G, c.head_dim) * 8) : 0;
   const size_t rcn = Q > 1 ? align256(size_t(BH) * 4) : 0;
   const size_t ra = align256(size_t(2) * BH * c.head_dim * 4);
-  x->arena_bytes = 2 * kv + 4 * sb + su + rp + rcn + ra + 256;
+  const bool slices = Q > 1 && (c.top_k > 128 || max_local_candidates(x) > sd::kAllKeysMax || x->C == 1);
+  x->mt = slices ? list_len(c.top_k, Q) : 0;
+  const size_t cl = slices ? align256(size_t(BH) * Q * x->mt * 2 * 8) : 0;
+  const size_t cf = slices ? align256(size_t(BH) * Q * c.top_k * 2 * 8) : 0;
+  x->arena_bytes = 2 * kv + 4 * sb + su + rp + rcn + cl + cf + ra + 256;
   cudaError_t e = cudaMalloc(&x->arena, x->arena_bytes);
   if (e != cudaSuccess) {
+    const size_t bytes = x->arena_bytes;
     delete x;
-    return fail(SD_ERR_CUDA, "cudaMalloc(%zu) failed: %s", x->arena_bytes, cudaGetErrorString(e));
+    return fail(SD_ERR_CUDA, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
   }
   uint8_t* a = static_cast<uint8_t*>(x->arena);
   x->k_data = a; a += kv;
@@ -485,6 +561,8 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
   x->summ = a; a += su;
   x->gslot = rp ? reinterpret_cast<unsigned long long*>(a) : nullptr; a += rp;
   x->gep = rcn ? reinterpret_cast<uint32_t*>(a) : nullptr; a += rcn;
+  x->clist = cl ? reinterpret_cast<unsigned long long*>(a) : nullptr; a += cl;
+  x->cfall = cf ? reinterpret_cast<unsigned long long*>(a) : nullptr; a += cf;
   x->racc = reinterpret_cast<float*>(a); a += ra;
   x->d_err = reinterpret_cast<int*>(a);
   e = cudaMemset(x->arena, 0, x->arena_bytes);
@@ -728,12 +806,13 @@ int32_t sd_comm_create(const sd_index* x, sd_comm** out) {
   m.P = c.shard_count; m.pr = c.shard_rank;
   m.BH = c.batch * c.n_kv_heads; m.K = c.top_k; m.C = x->C; m.R = x->R; m.G = x->G; m.D = c.head_dim;
   const int Q = m.C * m.R;
-  m.RS = 2 * m.G + (m.G * m.D + Q - 1) / Q;
+  const int NO = merge_owners(Q, m.G, m.D);
+  m.RS = merge_record(Q, m.G, m.D);
   m.resident = max_active_clusters(x, x->C) >= int64_t(m.BH) * x->R ? 1 : 0;
   const int64_t P = m.P, BH = m.BH;
   m.off_cand = 0;
   m.off_part = m.off_cand + int64_t(align256(size_t(P * BH * std::max(m.K, 1) * 2 * 8)));
-  m.off_ctl = m.off_part + int64_t(align256(size_t(P * BH * Q * m.RS * 8)));
+  m.off_ctl = m.off_part + int64_t(align256(size_t(P * BH * NO * m.RS * 8)));
   m.bytes = size_t(m.off_ctl) + 256;
   int dev = 0;
   SD_CUDA(cudaGetDevice(&dev));
@@ -883,7 +962,7 @@ int32_t sd_set_launch_overlap(sd_index* x, int32_t enable) {
 
 #ifdef SD_PHASE_TIMING
 // Phase-timing build only: decode launches of this index write their phase
-// stamps ([grid.y][grid.x][8] u64, see SD_STAMP_* in sd_device.cuh) to buf;
+// stamps ([grid.y][grid.x][16] u64, see SD_STAMP_* in sd_device.cuh) to buf;
 // NULL turns the stamps off.
 int32_t sd_debug_set_phase_buffer(sd_index* x, void* buf) {
   if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
@@ -999,6 +1078,7 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   x.cap_local = arrays->cap_local;
   x.nb_local = arrays->nb_local;
   x.cap_global = x.cap_local;
+  x.nb_global = x.nb_local;
   x.offset = offset;
   const int64_t BH = int64_t(c.batch) * c.n_kv_heads;
   if (BH * x.cap_local >= (int64_t(1) << 31) || BH > 65535)
@@ -1010,18 +1090,32 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   if (rc == SD_OK) rc = choose_cluster(&x);
   if (rc != SD_OK) return rc;
 
-  // Scratch layout: [0, 256) error word, then the groups' epochs, then the
-  // group merge's message words. Fewer replicas are used if the words do not
-  // fit. Both regions are cleared by every call (the array is shared by calls
-  // of any configuration, and a word left by another configuration could
-  // carry a matching epoch).
-  const int GD = x.G * c.head_dim;
-  auto slot_bytes = [&](int C, int R) {
+  // Scratch layout: [0, 256) reserved, then the groups' epochs, the group
+  // merge's message words and, for the sliced selection, the CTAs' lists.
+  // Fewer CTAs per group are used if they do not fit. Everything used is
+  // cleared by every call (the array is shared by calls of any configuration,
+  // and a word left by another configuration could carry a matching epoch).
+  const int64_t nloc = offset > c.block_size ? (offset + c.block_size - 1) / c.block_size - 1 : 0;
+  struct Need { size_t slots, lists, falls; int mt; };
+  auto need = [&](int C, int R) {
     const int Q = C * R;
-    return Q > 1 ? size_t(BH) * Q * Q * (2 * x.G + (GD + Q - 1) / Q) * 8 : size_t(0);
+    Need n{0, 0, 0, 0};
+    if (Q > 1) {
+      n.slots = align256(size_t(BH) * merge_owners(Q, x.G, c.head_dim) * Q * merge_record(Q, x.G, c.head_dim) * 8);
+      if (c.top_k > 128 || nloc > sd::kAllKeysMax || C == 1) {
+        n.mt = list_len(c.top_k, Q);
+        n.lists = align256(size_t(BH) * Q * n.mt * 2 * 8);
+        n.falls = align256(size_t(BH) * Q * c.top_k * 2 * 8);
+      }
+    }
+    return n;
   };
   const size_t ep_bytes = align256(size_t(BH) * 4);
-  auto fits = [&]() { return 256 + ep_bytes + slot_bytes(x.C, x.R) <= kNoAllocScratch; };
+  auto total = [&](int C, int R) {
+    const Need n = need(C, R);
+    return 256 + ep_bytes + n.slots + n.lists + n.falls;
+  };
+  auto fits = [&]() { return total(x.C, x.R) <= kNoAllocScratch; };
   // fewer replicas first, then smaller clusters (one CTA per group needs no message words)
   while (!fits() && x.R > 1) --x.R;
   while (!fits() && x.C > 1) {
@@ -1032,13 +1126,18 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   }
   if (!fits())
     return fail(SD_ERR_CAPACITY, "batch*kv_heads (%lld) needs %zu bytes of scratch; the limit is %zu",
-                (long long)BH, 256 + ep_bytes + slot_bytes(x.C, x.R), kNoAllocScratch);
+                (long long)BH, total(x.C, x.R), kNoAllocScratch);
+  const Need nd = need(x.C, x.R);
   void* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc != SD_OK) return rc;
   uint8_t* sb = static_cast<uint8_t*>(scratch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  SD_CUDA(cudaMemsetAsync(sb, 0, 256 + ep_bytes + slot_bytes(x.C, x.R), st));
+  SD_CUDA(cudaMemsetAsync(sb, 0, total(x.C, x.R), st));
+  x.mt = nd.mt;
+  x.gslot = nd.slots ? reinterpret_cast<unsigned long long*>(sb + 256 + ep_bytes) : nullptr;
+  x.clist = nd.lists ? reinterpret_cast<unsigned long long*>(sb + 256 + ep_bytes + nd.slots) : nullptr;
+  x.cfall = nd.falls ? reinterpret_cast<unsigned long long*>(sb + 256 + ep_bytes + nd.slots + nd.lists) : nullptr;
 
   x.k_data = arrays->k_data; x.v_data = arrays->v_data;
   x.k_scales = arrays->k_scales; x.k_biases = arrays->k_biases;
@@ -1067,11 +1166,16 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   p.sel_out = sel_out;
   p.err = device_flags;
   p.R = x.R;
+  p.nown = merge_owners(x.C * x.R, x.G, c.head_dim);
   p.gep = reinterpret_cast<uint32_t*>(sb + 256);
-  p.gslot = x.C * x.R > 1 ? reinterpret_cast<unsigned long long*>(sb + 256 + ep_bytes) : nullptr;
-  const int64_t nloc = p.NB - 1;
-  if ((nloc + x.C - 1) / x.C > sd::kLocalKeysMax)
-    return fail(SD_ERR_SHAPE, "too many blocks per CTA for cluster size %d", x.C);
+  p.gslot = x.gslot;
+  p.sliced = sliced_launch(&x, nloc) ? 1 : 0;
+  p.mt = x.mt;
+  p.clist = x.clist;
+  p.cfall = x.cfall;
+  const int64_t chunks = p.sliced ? int64_t(x.C) * x.R : x.C;
+  if ((nloc + chunks - 1) / chunks > sd::kLocalKeysMax)
+    return fail(SD_ERR_SHAPE, "too many blocks per CTA for %lld CTAs per group", (long long)chunks);
 
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(unsigned(x.C * x.R), unsigned(BH), 1);

@@ -112,6 +112,7 @@ __device__ __forceinline__ void consume_tiles_fma(const DecodeParams& p, const T
     const int s = i % F::kStages;
     if ((i < F::kStages || wait_issued(tw.issued, i, p.err)) &&
         mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
+      if (i == warp && warp == 0 && lane == 0) SD_STAMP_HERE(p, 9);
       const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
       const int nv = min(TS, T - (j * S + tile * TS));
       uint8_t* stage = tw.ring + s * F::kStageBytes;
@@ -280,6 +281,7 @@ __device__ __forceinline__ void consume_tiles_fma(const DecodeParams& p, const T
 #pragma unroll
       for (int e = 0; e < F::kDpl; ++e) o_acc[g][e] += ob[g][grp];
   }
+  if (warp == 0 && lane == 0) SD_STAMP_HERE(p, 10);
   named_barrier(1, kConsumerWarps * 32);  // all consumers are done with the ring
   float* w = tw.mw + warp * (G * D + 2 * G);
   if (lane == 0) {
@@ -330,6 +332,7 @@ __device__ __forceinline__ void consume_tiles_mma(const DecodeParams& p, const T
     const int s = i % F::kStages;
     if ((i < F::kStages || wait_issued(tw.issued, i, p.err)) &&
         mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
+      if (i == warp && warp == 0 && lane == 0) SD_STAMP_HERE(p, 9);
       const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
       const int nv = min(TS, T - (j * S + tile * TS));
       const uint32_t kb = smem_u32(tw.ring + s * F::kStageBytes);
@@ -400,6 +403,7 @@ __device__ __forceinline__ void consume_tiles_mma(const DecodeParams& p, const T
     __syncwarp();
     if (lane == 0) mbar_arrive(tw.empty + s);
   }
+  if (warp == 0 && lane == 0) SD_STAMP_HERE(p, 10);
   named_barrier(1, kConsumerWarps * 32);  // all consumers are done with the ring
   float* w = tw.mw + warp * (G * D + 2 * G);
   if (g < G) {
@@ -487,6 +491,7 @@ __device__ __forceinline__ void consume_tiles_qmma(const DecodeParams& p, const 
     const int s = i % F::kStages;
     if ((i < F::kStages || wait_issued(tw.issued, i, p.err)) &&
         mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
+      if (i == warp && warp == 0 && lane == 0) SD_STAMP_HERE(p, 9);
       const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
       const int nv = min(TS, T - (j * S + tile * TS));
       uint8_t* stage = tw.ring + s * F::kStageBytes;
@@ -616,6 +621,7 @@ __device__ __forceinline__ void consume_tiles_qmma(const DecodeParams& p, const 
     __syncwarp();
     if (lane == 0) mbar_arrive(tw.empty + s);
   }
+  if (warp == 0 && lane == 0) SD_STAMP_HERE(p, 10);
   named_barrier(1, kConsumerWarps * 32);  // all consumers are done with the ring
   float* w = tw.mw + warp * (G * D + 2 * G);
   if (g < G) {
@@ -703,17 +709,24 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
 
   const int ncand = NB - 1;  // candidate blocks [0, NB-1); the recent block is always taken
   const int nloc = ncand > pr ? (ncand - pr + P - 1) / P : 0;
-  // 32-bit: r * nloc <= 16 * 2^19 (the host bounds capacity and cluster size)
-  auto chunk_lo = [&](int r) { return r * nloc / C; };
-  const int c0 = chunk_lo(crank), c1 = chunk_lo(crank + 1);
+  // Whole selection (the host sets it for at most kAllKeysMax candidates,
+  // K <= 128 and clusters of several CTAs, or one CTA per group): each CTA of
+  // a cluster scores chunk crank of C and pushes the keys into every cluster
+  // peer's copy of the group's key array; after one cluster barrier every CTA
+  // selects by the same block-wide bitonic top-K (replica clusters repeat
+  // this; the keys are few). Otherwise the selection is sliced: every CTA of
+  // the group scores chunk qrank of Q, keeps its best keys, and the lists
+  // meet in L2.
+  const bool whole = p.mode != MODE_ATTEND && !p.sliced;
+  const int NCH = whole ? C : Q, ich = whole ? crank : qrank;
+  // 32-bit: r * nloc <= 64 * 2^19 (the host bounds capacity and group size)
+  auto chunk_lo = [&](int r) { return r * nloc / NCH; };
+  const int c0 = chunk_lo(ich), c1 = chunk_lo(ich + 1);
   const int n = c1 - c0;
   auto jglob = [&](int i) { return (c0 + i) * P + pr; };
-  // Up to kAllKeysMax candidates: each CTA scores its chunk and pushes the
-  // keys into every cluster peer's copy of the group's key array; after one
-  // cluster barrier every CTA selects by the same block-wide bitonic top-K.
-  const bool whole = p.mode != MODE_ATTEND && nloc <= kAllKeysMax && K <= 128;
   uint32_t* allk = reinterpret_cast<uint32_t*>(sm + L.allk);
   if (whole) keys = allk + c0;
+  else if (n <= kAllKeysMax) keys = allk;  // the ring stays free for the lists
   const int sc0 = c0, sn = n;  // the rows this CTA scores
 
   // Score-phase loads go out before the query barrier so that the two memory
@@ -721,8 +734,25 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   constexpr int LPB = F::kSumLanes, EPC = F::kSumEpc, BPW = 32 / LPB, UNR = 8, NWS = kConsumerWarps;
   const int sub = lane / LPB, cch = lane % LPB;
   const bool scorer = warp < NWS && p.mode != MODE_ATTEND;
-  const uint8_t* srow0 =
-      static_cast<const uint8_t*>(p.summ) + (size_t(bh) * p.nb_stride + sc0) * D * sizeof(E) + cch * 16;
+  const uint8_t* sbase = static_cast<const uint8_t*>(p.summ) + (size_t(bh) * p.nb_stride + sc0) * D * sizeof(E);
+  // The CTA's summary rows go to L2 at once: one bulk prefetch per 64 KB
+  // (thread 0; safe before the grid-dependency wait -- L2 is coherent and a
+  // prefetch never returns data), so the register batches below stream from
+  // L2 and HBM works on the whole chunk from the start.
+  if (p.mode != MODE_ATTEND && tid == 0 && sn > 0) {
+    constexpr int SROW = D * int(sizeof(E));
+    for (size_t off = 0; off < size_t(sn) * SROW; off += 65536)
+      bulk_prefetch_l2(sbase + off, uint32_t(min(size_t(65536), size_t(sn) * SROW - off)));
+  }
+  // Sliced selection with the keys in allk: the histogram of the keys'
+  // buckets that the top-K threshold search (topk_threshold) needs is built
+  // while scoring, in the ring.
+  uint32_t* hbk = reinterpret_cast<uint32_t*>(sm + L.ring + 128 * 1024);
+  const bool hist_scoring = !whole && K > 0 && keys != reinterpret_cast<uint32_t*>(sm + L.ring) &&
+                            p.mode != MODE_ATTEND;
+  if (hist_scoring)
+    for (int i = tid; i < kBuckets; i += kThreads) hbk[i] = 0u;
+  const uint8_t* srow0 = sbase + cch * 16;
   uint4 raw[UNR];
   if (scorer) {
 #pragma unroll
@@ -749,7 +779,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     }
   }
   // this launch's epoch of the group merge (the previous launch is complete)
-  const uint32_t gep = (Q > 1 && p.mode != MODE_CANDIDATES) ? __ldcg(p.gep + bh) + 1u : 0u;
+  const uint32_t gep = Q > 1 ? __ldcg(p.gep + bh) + 1u : 0u;
   const E* qg = static_cast<const E*>(p.q) + (size_t(b) * p.Hq + size_t(h) * G) * D;
   for (int i = tid; i < G * D; i += kThreads) {
     const int g = i / D, d = i % D;
@@ -806,6 +836,26 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       }
     }
   }
+  // one summary row's score (16-byte chunk per lane, canonical order) -> key
+  auto score_row = [&](const uint4& raw16, const float (&qr)[EPC], int i, bool valid) {
+    float f[EPC];
+    unpack_word<E>(raw16.x, f);
+    unpack_word<E>(raw16.y, f + EPC / 4);
+    unpack_word<E>(raw16.z, f + EPC / 2);
+    unpack_word<E>(raw16.w, f + 3 * EPC / 4);
+    float a = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPC; ++e) a = __fmaf_rn(qr[e], f[e], a);
+#pragma unroll
+    for (int o = LPB / 2; o >= 1; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (cch == 0 && valid) {
+      const float sc = __fmul_rn(a, p.scale);
+      const uint32_t key = score_key(sc);
+      keys[i] = key;
+      if (hist_scoring) atomicAdd(&hbk[key >> 20], 1u);
+      if (p.scores_out) p.scores_out[size_t(bh) * NB + size_t(sc0 + i) * P + pr] = sc;
+    }
+  };
   if (scorer) {
     float qr[EPC];
 #pragma unroll
@@ -825,21 +875,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
         const int i = it + u * NWS * BPW + sub;
-        float f[EPC];
-        unpack_word<E>(cur[u].x, f);
-        unpack_word<E>(cur[u].y, f + EPC / 4);
-        unpack_word<E>(cur[u].z, f + EPC / 2);
-        unpack_word<E>(cur[u].w, f + 3 * EPC / 4);
-        float a = 0.0f;
-#pragma unroll
-        for (int e = 0; e < EPC; ++e) a = __fmaf_rn(qr[e], f[e], a);
-#pragma unroll
-        for (int o = LPB / 2; o >= 1; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-        if (cch == 0 && i < sn) {
-          const float sc = __fmul_rn(a, p.scale);
-          keys[i] = score_key(sc);
-          if (p.scores_out) p.scores_out[size_t(bh) * NB + size_t(sc0 + i) * P + pr] = sc;
-        }
+        score_row(cur[u], qr, i, i < sn);
       }
     }
   }
@@ -858,6 +894,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   int kk;  // blocks chosen by top-K
   if (whole) {
     if (C > 1) cluster_sync();  // every peer's pushed keys have landed
+    SD_STAMP_C(p, 15);
     kk = min(K, nloc);
     if (nloc <= K || K == 0) {
       for (int i = tid; i < kk; i += kThreads) pick[i] = make_uint2(allk[i], uint32_t(i * P + pr));
@@ -866,6 +903,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       auto akey = [&](int i) -> unsigned long long { return full_key(allk[i], i * P + pr); };
       if (K <= 64) block_topk<2>(akey, nloc, runs, lane, warp, kThreads / 32);
       else block_topk<4>(akey, nloc, runs, lane, warp, kThreads / 32);
+      SD_STAMP_C(p, 14);
       for (int i = tid; i < kk; i += kThreads) {
         const unsigned long long x = runs[i];
         pick[i] = make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x));
@@ -873,137 +911,112 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     }
     __syncthreads();
   } else if (p.mode != MODE_ATTEND) {
-    // (1) This CTA's candidates (its top-K by radix select first when it holds
-    // more than kRunMax) are sorted in runs of 32 in registers and ranked
-    // against each other by binary search: this CTA's top-K, descending.
-    // (2) The lists are exchanged through DSMEM. (3) A candidate's rank in the
-    // group is its position in its own list plus the number of larger keys in
-    // every other list; selected = rank < K. The selected entries of a list
-    // are a prefix of it, so the ascending block order follows from per-list
-    // counts alone.
-    constexpr int kRunMax = 1024;
-    unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 64 * 1024);
-    unsigned long long* cand = reinterpret_cast<unsigned long long*>(sm + L.ring + 72 * 1024);
-    unsigned long long* lists = reinterpret_cast<unsigned long long*>(sm + L.ring + 80 * 1024);
-    uint8_t* flag = sm + L.ring + 144 * 1024;
-    int* llen = scratch + 64;   // per-rank list length
-    int* lbase = scratch + 80;  // per-rank offset in the union
-    int* cnt = scratch + 96;    // per-rank selected count
-    if (tid == 0) {
-      int acc = 0, kmax = 0;
-      for (int r = 0; r < C; ++r) {
-        llen[r] = min(K, chunk_lo(r + 1) - chunk_lo(r));
-        lbase[r] = acc;
-        acc += llen[r];
-        kmax = max(kmax, llen[r]);
-      }
-      scratch[112] = acc;   // U: union size
-      scratch[113] = kmax;  // list slot stride
-    }
-    if (tid < C) cnt[tid] = 0;
+    // Sliced selection. (1) This CTA's best min(n, MT) keys of its chunk
+    // (radix select when it holds more), in index order. (2) The list goes to
+    // L2 as message words tagged with the group's launch epoch. (3) Every CTA
+    // gathers the group's Q lists, drops the padding and finds the top-K of
+    // their union by radix select: the same set on every CTA. (4) The union
+    // holds the group's top-K unless some CTA had more than MT candidates and
+    // all MT of them made the union's top-K (its next key might belong too);
+    // then every CTA publishes its full top-K list and the selection is made
+    // again over those. The decision depends only on the gathered lists, so
+    // every CTA takes the same branch.
+    const int MT = p.mt;
+    unsigned long long* lst = reinterpret_cast<unsigned long long*>(sm + L.ring + 144 * 1024);  // <= kMaxTopK
+    int* bidx = reinterpret_cast<int*>(sm + L.ring + 152 * 1024);                              // 2048 ints
     auto keyf = [&](int i) -> unsigned long long { return full_key(keys[i], jglob(i)); };
-    int nsrc = n;
-    bool from_cand = false;
-    if (K > 0 && n > kRunMax) {
-      radix_select(keyf, n, K, hist, rs);
-      const unsigned long long pre = rs->prefix, msk = rs->mask;
-      cta_compact(n, [&](int i) { return (keyf(i) & msk) >= pre; }, [&](int pos, int i) { cand[pos] = keyf(i); },
-                  scratch);
-      nsrc = K;
-      from_cand = true;
-    }
-    __syncthreads();
-    const int U = scratch[112];
-    const int KS = max(scratch[113], 1);
-    const int kr = min(K, nsrc);
-    unsigned long long* mine = lists + crank * KS;
-    if (kr > 0) {
-      const int nrun = (nsrc + 31) / 32;
-      for (int rr = warp; rr < nrun; rr += kThreads / 32) {
-        const int i = rr * 32 + lane;
-        unsigned long long x = 0ull;
-        if (i < nsrc) x = from_cand ? cand[i] : keyf(i);
-        runs[rr * 32 + lane] = warp_sort_desc(x, lane);
+    // this CTA's best m keys, in index order; returns how many. The bucket
+    // histogram of the keys is the one built while scoring the first time.
+    bool hist_ready = hist_scoring;
+    auto local_list = [&](int m) {
+      if (n > m && m > 0) {
+        const unsigned long long tau = topk_threshold(keyf, n, m, hbk, hist_ready, bidx, 2048, scratch, hist, rs);
+        hist_ready = false;
+        cta_compact(n, [&](int i) { return keyf(i) >= tau; }, [&](int pos, int i) { lst[pos] = keyf(i); }, scratch);
+      } else {
+        for (int i = tid; i < min(n, m); i += kThreads) lst[i] = keyf(i);
+        __syncthreads();
       }
+      return min(n, m);
+    };
+    auto to_pick = [](unsigned long long x) { return make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x)); };
+    if (K == 0) {
+      kk = 0;
+    } else if (Q == 1) {
+      kk = local_list(K);
+      for (int i = tid; i < kk; i += kThreads) pick[i] = to_pick(lst[i]);
       __syncthreads();
-      for (int i = tid; i < nsrc; i += kThreads) {
-        const unsigned long long x = runs[i];
-        const int ra = i >> 5;
-        int rank = i & 31;
-        for (int rb = 0; rb < nrun; ++rb)
-          if (rb != ra) rank += count_greater(runs + rb * 32, min(32, nsrc - rb * 32), x);
-        if (rank < kr) mine[rank] = x;
-      }
-    }
-    __syncthreads();
-    // Every CTA ranks only its own list against the others (pulled through
-    // DSMEM after one barrier) and publishes how many of its entries made the
-    // group's top-K (a prefix of its list) with a second barrier.
-    int* rank_own = reinterpret_cast<int*>(flag);  // kr ints (flag area is free here)
-    for (int i = tid; i < kr; i += kThreads) rank_own[i] = i;
-    if (C > 1) {
-      cluster_sync();
-      // one flat pass over the union: every remote load in flight before any store
-      const uint32_t la = smem_u32(lists);
-      for (int ub = tid; ub < U; ub += kThreads * 4) {
-        uint32_t lo[4], hi[4];
-        int dst[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int u = ub + k * kThreads;
-          dst[k] = -1;
-          if (u < U) {
-            int r = 0;
-            while (r + 1 < C && u >= lbase[r + 1]) ++r;
-            if (r != crank) {
-              dst[k] = r * KS + (u - lbase[r]);
-              const uint32_t ra = map_rank(la + uint32_t(dst[k]) * 8u, uint32_t(r));
-              asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];" : "=r"(lo[k]), "=r"(hi[k]) : "r"(ra));
-            }
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if (dst[k] >= 0) lists[dst[k]] = (uint64_t(hi[k]) << 32) | lo[k];
-      }
-      __syncthreads();
-      for (int item = tid; item < kr * C; item += kThreads) {
-        const int i = item / C, r2 = item - i * C;
-        if (r2 == crank) continue;
-        const int c = count_greater(lists + r2 * KS, llen[r2], mine[i]);
-        if (c) atomicAdd(&rank_own[i], c);
-      }
-    }
-    __syncthreads();
-    // selected entries of this CTA's list: the prefix with rank < K
-    for (int i = tid; i < kr; i += kThreads) {
-      const bool in = rank_own[i] < K;
-      const bool next_in = i + 1 < kr && rank_own[i + 1] < K;
-      if (in && !next_in) scratch[115] = i + 1;
-    }
-    if (tid == 0 && (kr == 0 || rank_own[0] >= K)) scratch[115] = 0;
-    __syncthreads();
-    if (C > 1) {
-      const int c_own = scratch[115];
-      if (tid < C) st_cluster_u32(map_rank(smem_u32(&cnt[crank]), uint32_t(tid)), uint32_t(c_own));
-      cluster_sync();
     } else {
-      if (tid == 0) cnt[0] = scratch[115];
+      // publish this CTA's list (0-padded to m key pairs) and gather all Q
+      // lists into g[0, 2*Q*m) (u32 halves of the keys)
+      auto exchange = [&](unsigned long long* area, int m, int nl, uint32_t* g) {
+        unsigned long long* mine = area + size_t(qrank) * m * 2;
+        for (int i = tid; i < m; i += kThreads) {
+          const unsigned long long x = i < nl ? lst[i] : 0ull;
+          st_msg_gpu(mine + 2 * i, uint32_t(x >> 32), gep);
+          st_msg_gpu(mine + 2 * i + 1, uint32_t(x), gep);
+        }
+        gather_msgs<false>([&](int i) { return area + i; }, Q * m * 2, gep, kWaitLimitNs, p.err,
+                           reinterpret_cast<float*>(g), tid, kThreads, [](int) { return true; });
+        __syncthreads();
+      };
+      // the union's non-zero keys, compacted into u[] as (score key, block);
+      // tau = its K-th largest key when it holds more than K (else 0: all)
+      unsigned long long tau = 0ull;
+      auto union_topk = [&](const uint32_t* g, int N, uint2* u) {
+        auto gk = [&](int i) { return (static_cast<unsigned long long>(g[2 * i]) << 32) | g[2 * i + 1]; };
+        const int U = cta_compact(N, [&](int i) { return gk(i) != 0ull; },
+                                  [&](int pos, int i) { u[pos] = to_pick(gk(i)); }, scratch);
+        tau = 0ull;
+        if (U > K) {
+          auto ukey = [&](int i) -> unsigned long long { return full_key(u[i].x, int32_t(u[i].y)); };
+          tau = topk_threshold(ukey, U, K, hbk, false, bidx, 2048, scratch, hist, rs);
+        }
+        return U;
+      };
+      uint32_t* g1 = reinterpret_cast<uint32_t*>(sm + L.ring + 64 * 1024);  // 2*Q*MT u32 (<= 32 KB)
+      uint2* u1 = reinterpret_cast<uint2*>(sm + L.ring + 96 * 1024);        // <= Q*MT pairs (<= 32 KB)
+      const int nl1 = local_list(MT);
+      SD_STAMP_C(p, 15);
+      exchange(p.clist + size_t(bh) * Q * MT * 2, MT, nl1, g1);
+      SD_STAMP_C(p, 14);
+      int U = union_topk(g1, Q * MT, u1);
+      uint2* u = u1;
+      bool fallback = false;
+      if (MT < K) {
+        // lists whose CTA had more than MT candidates and whose MT entries are
+        // all selected
+        for (int i = tid; i < Q; i += kThreads) hist[i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < Q * MT; i += kThreads) {
+          const unsigned long long x = (static_cast<unsigned long long>(g1[2 * i]) << 32) | g1[2 * i + 1];
+          if (x != 0ull && x >= tau) atomicAdd(&hist[i / MT], 1u);
+        }
+        __syncthreads();
+        int need = 0;
+        for (int q = tid; q < Q; q += kThreads) need |= (chunk_lo(q + 1) - chunk_lo(q) > MT && int(hist[q]) == MT);
+        fallback = __syncthreads_or(need) != 0;
+      }
+      if (fallback) {
+        uint32_t* g2 = reinterpret_cast<uint32_t*>(sm + L.ring);              // 2*Q*K u32 (<= 64 KB)
+        uint2* u2 = reinterpret_cast<uint2*>(sm + L.ring + 64 * 1024);        // <= Q*K pairs (<= 64 KB)
+        const int nl = local_list(K);  // the keys are intact: they live below 64 KB or in allk
+        exchange(p.cfall + size_t(bh) * Q * K * 2, K, nl, g2);
+        U = union_topk(g2, Q * K, u2);
+        u = u2;
+      }
+      // CANDIDATES mode ends before the group merge, whose owner 0 advances
+      // the epoch: CTA 0 holds every list, so every CTA has read the epoch.
+      if (p.mode == MODE_CANDIDATES && qrank == 0 && tid == 0) p.gep[bh] = gep;
+      kk = min(K, U);
+      if (U > K) {
+        cta_compact(U, [&](int i) { return full_key(u[i].x, int32_t(u[i].y)) >= tau; },
+                    [&](int pos, int i) { pick[pos] = u[i]; }, scratch);
+      } else {
+        for (int i = tid; i < kk; i += kThreads) pick[i] = u[i];
+        __syncthreads();
+      }
     }
-    __syncthreads();
-    kk = min(K, U);
-    // the selection in list order (rank by rank, key order inside a list);
-    // the ascending order that sel_out reports is produced off the critical
-    // path by the producer warp
-    for (int item = tid; item < C * KS; item += kThreads) {
-      const int r = item / KS, i = item - r * KS;
-      if (i >= cnt[r]) continue;
-      int before = 0;
-      for (int r2 = 0; r2 < r; ++r2) before += cnt[r2];
-      const unsigned long long x = lists[r * KS + i];
-      pick[before + i] = make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x));
-    }
-    __syncthreads();
   }
   // The group's top-K of a candidate union uni[0, U) (score key, block), by
   // radix select; every shard computes the same selection.
@@ -1200,6 +1213,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       fence_proxy_async_shared();
       fence_proxy_async_global();
       for (int i = 0; i < min(nmine, F::kStages); ++i) issue(i);
+      SD_STAMP_HERE(p, 8);
     }
     __syncwarp();
     // sel_out: the selected blocks ascending (rank counting), recent last, -1 padded
@@ -1258,17 +1272,23 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     for (int w = 0; w < kConsumerWarps; ++w) O += mw[w * WSTRIDE + 2 * G + idx] * wf[w * G + g];
     cpart[2 * G + idx] = O;
   }
-  // The group's Q = C*R CTAs merge through L2: output elements are cut into Q
-  // slices, CTA q owns slice q. Every CTA sends each owner a record -- the
-  // (m, l) of every head, then its partial o over the owner's slice -- as
-  // message words tagged with the group's launch epoch; each owner reads the
-  // Q records of its slice as their words arrive and merges them in CTA
-  // order. All Q CTAs are resident at once (clusters, or replica clusters
-  // chosen so that all fit), so the owners' bounded waits always end.
+  // The group's Q = C*R CTAs merge through L2: output elements are cut into
+  // NO slices (NO = p.nown <= Q, host-chosen so that an owner gathers its
+  // records in one batch of loads), CTA q < NO owns slice q. Every CTA sends
+  // each owner a record -- the (m, l) of every head, then its partial o over
+  // the owner's slice -- as message words tagged with the group's launch
+  // epoch; each owner reads the Q records of its slice as their words arrive
+  // and merges them in CTA order. The other CTAs are done once their records
+  // are out: they exit early, and a programmatically dependent next launch
+  // can start its prologue on their SMs. All Q CTAs are resident at once
+  // (clusters, or replica clusters chosen so that all fit), so the owners'
+  // bounded waits always end.
   constexpr int GD = G * D;
-  const int SL = (GD + Q - 1) / Q;   // slice length
+  const int NO = Q > 1 ? p.nown : 1;
+  const int SL = (GD + NO - 1) / NO;  // slice length
   const int RS = 2 * G + SL;          // record length (words)
-  const int e0 = min(GD, qrank * SL), e1 = min(GD, e0 + SL);
+  const bool owner = qrank < NO;
+  const int e0 = owner ? min(GD, qrank * SL) : GD, e1 = owner ? min(GD, e0 + SL) : GD;
   const int g0 = e0 / D, g1 = (e1 - 1) / D;  // heads this slice touches
   auto emit = [&](int idx, float M, float Ls, float O) {
     const int g = idx / D, d = idx % D;
@@ -1278,7 +1298,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     } else if (peer) {
       // this shard's record of (group, slice) -- [2G (m, l)][slice of o] as
       // message words -- into every shard's exchange area
-      const size_t ro = ((size_t(pr) * gridDim.y + bh) * Q + qrank) * RS;
+      const size_t ro = ((size_t(pr) * gridDim.y + bh) * NO + qrank) * RS;
       for (int r = 0; r < P; ++r) {
         unsigned long long* rec = reinterpret_cast<unsigned long long*>(p.peer[r] + p.x_part) + ro;
         st_msg(rec + 2 * G + idx - e0, __float_as_uint(O), epoch);
@@ -1293,20 +1313,22 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     }
   };
   __syncthreads();  // cpart is complete
+  SD_STAMP_C(p, 11);
   if (Q == 1) {
     for (int idx = e0 + tid; idx < e1; idx += kThreads) {
       const int g = idx / D;
       emit(idx, cpart[g], cpart[G + g], cpart[2 * G + idx]);
     }
   } else {
-    unsigned long long* slots = p.gslot + size_t(bh) * Q * Q * RS;  // [owner][source][RS]
-    for (int i = tid; i < Q * RS; i += kThreads) {
+    unsigned long long* slots = p.gslot + size_t(bh) * NO * Q * RS;  // [owner][source][RS]
+    for (int i = tid; i < NO * RS; i += kThreads) {
       const int o = i / RS, k = i - o * RS;
       const int e = o * SL + (k - 2 * G);
       if (k >= 2 * G && e >= GD) continue;
       st_msg_gpu(slots + (size_t(o) * Q + qrank) * RS + k, __float_as_uint(k < 2 * G ? cpart[k] : cpart[2 * G + e]),
                  gep);
     }
+    SD_STAMP_C(p, 12);
     // as the owner of [e0, e1): every source's record, gathered into shared
     // memory with all loads of a batch in flight at once (the ring is free)
     const unsigned long long* mine = slots + size_t(qrank) * Q * RS;
@@ -1317,9 +1339,11 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       const int g = k % G;
       return nw > 0 && g >= g0 && g <= g1;
     };
-    gather_msgs<false>([&](int i) { return mine + i; }, Q * RS, gep, kWaitLimitNs, p.err, rq, tid, kThreads,
-                       [&](int i) { return needed(i % RS); });
+    if (owner)
+      gather_msgs<false>([&](int i) { return mine + i; }, Q * RS, gep, kWaitLimitNs, p.err, rq, tid, kThreads,
+                         [&](int i) { return needed(i % RS); });
     __syncthreads();
+    SD_STAMP_C(p, 13);
     for (int idx = e0 + tid; idx < e1; idx += kThreads) {
       const int g = idx / D;
       float M = -INFINITY;
@@ -1352,12 +1376,13 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   {
     const int BHn = int(gridDim.y);
     const unsigned long long* recs = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_part);
-    auto rec = [&](int r) { return recs + ((size_t(r) * BHn + bh) * Q + qrank) * RS; };
+    auto rec = [&](int r) { return recs + ((size_t(r) * BHn + bh) * NO + qrank) * RS; };
     float* rp = reinterpret_cast<float*>(sm + L.ring + 32 * 1024);  // [P][RS] (the ring is free)
     const int nw = e1 - e0;
     __syncthreads();  // the group merge above may still read the ring
-    gather_msgs<true>([&](int i) { return rec(i / RS) + (i % RS); }, P * RS, epoch, p.peer_wait_ns, p.err, rp, tid,
-                      kThreads, [&](int i) {
+    if (owner)
+      gather_msgs<true>([&](int i) { return rec(i / RS) + (i % RS); }, P * RS, epoch, p.peer_wait_ns, p.err, rp, tid,
+                        kThreads, [&](int i) {
                         const int k = i % RS;
                         if (k >= 2 * G) return k - 2 * G < nw;
                         const int g = k % G;

@@ -127,29 +127,39 @@ __device__ __forceinline__ uint64_t globaltimer() {
 }
 
 // Phase stamps of the decode kernel, compiled only into the phase-timing
-// build (-DSD_PHASE_TIMING): thread 0 of every CTA writes 8 u64 per CTA to
-// DecodeParams::dbg -- [0] %globaltimer at entry, [1..6] clock64 at entry,
-// scoring start, scoring end, selection end, attention end, merge end, [7]
-// %globaltimer at exit. The product build has no stamps.
+// build (-DSD_PHASE_TIMING): 16 u64 per CTA in DecodeParams::dbg. Thread 0
+// writes [0] %globaltimer at entry and [7] at exit, and clock64 at [1] entry,
+// [2] scoring start, [3] scoring end, [4] selection end, [5] attention end,
+// [6] merge end; [14]/[15] inside the selection (the local list / the
+// exchange). One thread of the producer warp writes [8] (first ring fill
+// issued), consumer warp 0's lane 0 [9] (its first tile arrived) and [10]
+// (its last tile done), thread 0 [11] (partials written), [12] (merge
+// records stored) and [13] (merge records gathered). The product build has
+// no stamps.
 #ifdef SD_PHASE_TIMING
 __device__ __forceinline__ unsigned long long clock_u64() {
   unsigned long long c;
   asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
   return c;
 }
-#define SD_STAMP_T(p, k)                                                                   \
-  do {                                                                                     \
-    if (threadIdx.x == 0 && (p).dbg)                                                        \
-      (p).dbg[(size_t(blockIdx.y) * gridDim.x + blockIdx.x) * 8 + (k)] = ::sd::globaltimer(); \
+#define SD_DBG_SLOT(p, k) (p).dbg[(size_t(blockIdx.y) * gridDim.x + blockIdx.x) * 16 + (k)]
+#define SD_STAMP_T(p, k)                                             \
+  do {                                                               \
+    if (threadIdx.x == 0 && (p).dbg) SD_DBG_SLOT(p, k) = ::sd::globaltimer(); \
   } while (0)
-#define SD_STAMP_C(p, k)                                                                   \
-  do {                                                                                     \
-    if (threadIdx.x == 0 && (p).dbg)                                                        \
-      (p).dbg[(size_t(blockIdx.y) * gridDim.x + blockIdx.x) * 8 + (k)] = ::sd::clock_u64();   \
+#define SD_STAMP_C(p, k)                                             \
+  do {                                                               \
+    if (threadIdx.x == 0 && (p).dbg) SD_DBG_SLOT(p, k) = ::sd::clock_u64(); \
+  } while (0)
+// clock64 from the calling thread (the caller picks one thread)
+#define SD_STAMP_HERE(p, k)                                          \
+  do {                                                               \
+    if ((p).dbg) SD_DBG_SLOT(p, k) = ::sd::clock_u64();              \
   } while (0)
 #else
 #define SD_STAMP_T(p, k) do { } while (0)
 #define SD_STAMP_C(p, k) do { } while (0)
+#define SD_STAMP_HERE(p, k) do { } while (0)
 #endif
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -278,6 +288,12 @@ __device__ __forceinline__ void gather_msgs(Addr addr, int n, uint32_t epoch, ui
       }
     }
   }
+}
+
+// Bulk L2 prefetch of [p, p + bytes) (16-byte aligned, bytes % 16 == 0) by the
+// TMA unit: one instruction for a long contiguous range.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // Generic-proxy writes -> async-proxy (TMA) reads ordering.
@@ -689,6 +705,85 @@ __device__ void radix_select(KeyF keyf, int n, int k, uint32_t* hist, RadixState
   }
   if (tid == 0) { st->prefix = prefix; st->mask = mask; }
   __syncthreads();
+}
+
+// Buckets of the top-K threshold search: the top 12 bits of a 64-bit key
+// (sign, exponent and 3 mantissa bits of the score).
+constexpr int kBuckets = 4096;
+__device__ __forceinline__ uint32_t key_bucket(unsigned long long x) { return uint32_t(x >> 52); }
+
+// The k-th largest of n distinct 64-bit keys keyf(i) (0 < k < n), i.e. the
+// threshold tau with exactly k keys >= tau. A histogram of the keys' buckets
+// (`h`, kBuckets u32 of shared memory; filled here unless the caller built it
+// already) finds the bucket that holds the k-th key; the keys of that bucket
+// (usually a few dozen) are compacted into bidx (room for cap / 2 keys) and
+// ranked against each other by counting. When the bucket holds more than
+// min(cap / 2, 256) keys
+// (equal scores, say) a radix select over all n keys decides instead. All CTA
+// threads call; scratch: cta_exclusive_scan's 33 ints plus [120, 124).
+template <class KeyF>
+__device__ unsigned long long topk_threshold(KeyF keyf, int n, int k, uint32_t* h, bool have_hist, int* bidx,
+                                             int cap, int* scratch, uint32_t* hist256, RadixState* rs) {
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  unsigned long long* tau = reinterpret_cast<unsigned long long*>(scratch + 122);
+  if (!have_hist) {
+    for (int i = tid; i < kBuckets; i += nthr) h[i] = 0u;
+    __syncthreads();
+    for (int i = tid; i < n; i += nthr) atomicAdd(&h[key_bucket(keyf(i))], 1u);
+  }
+  __syncthreads();
+  // each thread sums a run of buckets from the top; the run holding the k-th
+  // key finds its bucket b and the count above it
+  const int per = (kBuckets + nthr - 1) / nthr;
+  const int top = kBuckets - 1 - tid * per;
+  int cnt = 0;
+  for (int j = 0; j < per; ++j)
+    if (top - j >= 0) cnt += int(h[top - j]);
+  int total;
+  const int before = cta_exclusive_scan(cnt, scratch, &total);
+  if (before < k && before + cnt >= k) {
+    int acc = before;
+    for (int j = 0; j < per && top - j >= 0; ++j) {
+      const int c = int(h[top - j]);
+      if (acc + c >= k) {
+        scratch[120] = top - j;
+        scratch[121] = acc;
+        break;
+      }
+      acc += c;
+    }
+  }
+  if (tid == 0) *tau = ~0ull;
+  __syncthreads();
+  const uint32_t b = uint32_t(scratch[120]);
+  const int r = k - scratch[121];  // keys still needed from bucket b (>= 1)
+  const int nb = int(h[b]);
+  if (nb <= min(cap / 2, 256)) {
+    // the bucket's keys, compacted as keys (bidx holds 2 ints per key)
+    unsigned long long* bk = reinterpret_cast<unsigned long long*>(bidx);
+    cta_compact(n, [&](int i) { return key_bucket(keyf(i)) == b; }, [&](int pos, int i) { bk[pos] = keyf(i); },
+                scratch);
+    for (int a = tid; a < nb; a += nthr) {
+      const unsigned long long x = bk[a];
+      int rank = 0;
+#pragma unroll 8
+      for (int c = 0; c < nb; ++c) rank += bk[c] > x ? 1 : 0;  // every thread reads the same word: broadcast
+      if (rank == r - 1) *tau = x;
+    }
+  } else {
+    radix_select(keyf, n, k, hist256, rs);
+    const unsigned long long pre = rs->prefix, msk = rs->mask;
+    unsigned long long m = ~0ull;
+    for (int i = tid; i < n; i += nthr) {
+      const unsigned long long x = keyf(i);
+      if ((x & msk) >= pre && x < m) m = x;
+    }
+    atomicMin(tau, m);
+  }
+  __syncthreads();
+  const unsigned long long t = *tau;
+  __syncthreads();
+  return t;
 }
 
 }  // namespace sd

@@ -36,8 +36,16 @@ struct DecodeParams {
   float* part_o;          // attend mode: out [B*Hq, D] unnormalised
   int* err;               // device error word (sd::kErr*)
   int R;                  // replica clusters per (b, kv-head): each attends 1/R of the tiles
-  unsigned long long* gslot;  // Q = C*R > 1: [BH][Q owners][Q sources][2G + ceil(G*D/Q)] message words
+  int nown;               // Q = C*R > 1: CTAs of a group that own a slice of the output (the merge)
+  unsigned long long* gslot;  // Q = C*R > 1: [BH][nown owners][Q sources][2G + ceil(G*D/nown)] message words
   uint32_t* gep;          // Q > 1: [BH] epoch of each group's last merged launch
+  // Sliced selection (more than kAllKeysMax candidates per group, or K > 128)
+  // with Q > 1: every CTA's best mt keys [BH][Q][mt][2] and, when a list ran
+  // out, every CTA's full top-K [BH][Q][K][2], as message words.
+  int sliced;             // 1: the sliced selection (set per launch by the host)
+  int mt;
+  unsigned long long* clist;
+  unsigned long long* cfall;
   int pdl_early;          // 1: this index's summaries may be read before the grid-dependency wait
   const float* racc_in;   // [BH, D] fp32 sum of the recent block's rows before this step
   float* racc_out;        // [BH, D] the same sum after the appended row
@@ -46,7 +54,7 @@ struct DecodeParams {
   // Peer mode: every shard's exchange area mapped into this process (own at
   // [pr]). Area layout, identical on every shard, all message words (32-bit
   // payload | epoch << 32): [P][BH][K][2] candidate keys (hi, lo) at x_cand,
-  // [P][BH][C][RSZ] partial records ([2G] (m, l), then the slice of o) at
+  // [P][BH][nown][RS] partial records ([2G] (m, l), then the slice of o) at
   // x_part; at x_ctl two u32 control words of this shard: the last finished
   // epoch and the count of finished CTAs.
   uint8_t* peer[8];
@@ -56,7 +64,7 @@ struct DecodeParams {
   // v_scales, v_biases at one fixed stride), one copy per tile. 0: four 1-D
   // bulk copies.
   int sb_fused;
-  unsigned long long* dbg;  // phase-timing build only: [grid.y][grid.x][8] stamps, or null
+  unsigned long long* dbg;  // phase-timing build only: [grid.y][grid.x][16] stamps, or null
 };
 
 struct AppendParams {

@@ -7,8 +7,9 @@ selection end, attention end, merge end). This module builds `layers`
 independent single-layer indexes of a workload exactly as bench.py does,
 captures one decode step of all of them in a CUDA graph, replays it, and
 reports per phase the median and maximum over CTAs (microseconds, clock64
-cycles converted with each CTA's own cycles-per-ns), plus the layer cadence
-seen by %globaltimer.
+cycles converted with each CTA's own cycles-per-ns), sub-phases of the
+selection, attention and merge (medians; a sub-phase whose stamps a path
+does not write is left out), plus the layer cadence seen by %globaltimer.
 
     python -m sparse_decode.phase_profile --config c1 --layers 36
 
@@ -26,11 +27,18 @@ import sys
 from pathlib import Path
 
 PHASES = ["prologue", "score", "select", "attend", "merge"]
+# sub-phases: (name, from slot, to slot) -- see SD_STAMP_* in csrc/sd_device.cuh
+SUBPHASES = [("select.local_or_cluster_wait", 3, 15), ("select.exchange_or_topk", 15, 14), ("select.rest", 14, 4),
+             ("attend.first_fill_issued", 4, 8), ("attend.warp0_first_tile", 4, 9), ("attend.warp0_tiles", 9, 10),
+             ("attend.tail", 10, 5), ("merge.cta_partial", 5, 11), ("merge.store", 11, 12),
+             ("merge.gather", 12, 13), ("merge.output", 13, 6)]
 
 
 def _load_phase_lib():
     from . import build as b
-    path = b.LIB_PHASES if b.LIB_PHASES.exists() else b.build(phase_timing=True)
+    # SPARSE_DECODE_LIB may name another phase-timing build to profile
+    path = os.environ.get("SPARSE_DECODE_LIB") or (b.LIB_PHASES if b.LIB_PHASES.exists()
+                                                   else b.build(phase_timing=True))
     os.environ["SPARSE_DECODE_LIB"] = str(path)
     import sparse_decode
     if sparse_decode._lib is not None and not hasattr(sparse_decode._lib, "sd_debug_set_phase_buffer"):
@@ -61,7 +69,7 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True) -> 
         idx.set_launch_overlap(overlap)
         gx, gy = ctypes.c_int32(), ctypes.c_int32()
         _check(L.sd_debug_grid(idx._h, ctypes.byref(gx), ctypes.byref(gy)))
-        buf = torch.zeros((gy.value, gx.value, 8), dtype=torch.int64, device="cuda")
+        buf = torch.zeros((gy.value, gx.value, 16), dtype=torch.int64, device="cuda")
         _check(L.sd_debug_set_phase_buffer(idx._h, ctypes.c_void_p(buf.data_ptr())))
         items.append({"idx": idx, "q": case["q"].contiguous(), "k": k[:, :, w.T - 1].contiguous(),
                       "v": v[:, :, w.T - 1].contiguous(), "out": torch.empty_like(case["q"]), "buf": buf})
@@ -91,20 +99,28 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True) -> 
 
     per_phase = {p: [] for p in PHASES}
     per_phase_max = {p: [] for p in PHASES}
+    per_sub = {n: [] for n, _, _ in SUBPHASES}
     spans, entries, exits, skews = [], [], [], []
     for it in items:
-        a = it["buf"].cpu().reshape(-1, 8).tolist()
+        a = it["buf"].cpu().reshape(-1, 16).tolist()
         ph = {p: [] for p in PHASES}
+        sub = {n: [] for n, _, _ in SUBPHASES}
         for r in a:
-            gt0, c1, c2, c3, c4, c5, c6, gt7 = r
+            gt0, c1, c2, c3, c4, c5, c6, gt7 = r[:8]
             ns = gt7 - gt0
             cyc = c6 - c1
             cpn = cyc / ns if ns > 0 else 1.965
             for p_, (x, y) in zip(PHASES, [(c1, c2), (c2, c3), (c3, c4), (c4, c5), (c5, c6)]):
                 ph[p_].append((y - x) / cpn / 1000.0)
+            for n_, x, y in SUBPHASES:
+                if r[x] and r[y]:
+                    sub[n_].append((r[y] - r[x]) / cpn / 1000.0)
         for p_ in PHASES:
             per_phase[p_].append(statistics.median(ph[p_]))
             per_phase_max[p_].append(max(ph[p_]))
+        for n_, _, _ in SUBPHASES:
+            if sub[n_]:
+                per_sub[n_].append(statistics.median(sub[n_]))
         t0 = min(r[0] for r in a)
         t1 = max(r[7] for r in a)
         entries.append(t0)
@@ -119,6 +135,7 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True) -> 
         "algorithmic_bytes_per_layer": algorithmic_bytes(w),
         "phase_us_median_over_ctas": {p: round(statistics.median(per_phase[p]), 3) for p in PHASES},
         "phase_us_max_over_ctas": {p: round(statistics.median(per_phase_max[p]), 3) for p in PHASES},
+        "subphase_us_median": {n: round(statistics.median(v), 3) for n, v in per_sub.items() if v},
         "layer_span_us": round(statistics.median(spans), 3),
         "cta_start_skew_us": round(statistics.median(skews), 3),
         "layer_cadence_us": round(statistics.median(cad), 3) if cad else None,
