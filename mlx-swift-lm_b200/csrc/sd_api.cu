@@ -123,6 +123,8 @@ struct sd_index {
   const float* sinks;   // [Hq] attention-sink logits (device), or null
   CUtensorMap tmK, tmV, tmS;
   int sb_fused;         // tmS covers the four scale/bias arrays
+  int lt;               // tokens per staged copy
+  int kv_fused;         // tmK covers V too (4-D)
   sd::KernelSet ks;
   bool attrs_set;
   unsigned long long* dbg;  // phase-timing build: stamp buffer of the decode launches
@@ -177,7 +179,7 @@ int32_t validate(const sd_config* c) {
 // its boxes, landing as [box][row][box bytes] in shared memory. One TMA
 // operation per tile rather than one per box: the SM's TMA unit spends a fixed
 // time on each operation, which dominates copies of a few KB.
-int32_t encode_map(CUtensorMap* map, void* base, int row_bytes, int64_t rows) {
+int32_t encode_map(CUtensorMap* map, void* base, int row_bytes, int64_t rows, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(SD_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const int box_bytes = std::min(row_bytes, 128);
@@ -187,13 +189,42 @@ int32_t encode_map(CUtensorMap* map, void* base, int row_bytes, int64_t rows) {
                                             : CU_TENSOR_MAP_SWIZZLE_32B;
   cuuint64_t dims[3] = {cuuint64_t(box_bytes), cuuint64_t(rows), cuuint64_t(nbox)};
   cuuint64_t strides[2] = {cuuint64_t(row_bytes), cuuint64_t(box_bytes)};
-  cuuint32_t box[3] = {cuuint32_t(box_bytes), cuuint32_t(sd::kTileTokens), cuuint32_t(nbox)};
+  cuuint32_t box[3] = {cuuint32_t(box_bytes), cuuint32_t(box_rows), cuuint32_t(nbox)};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
   return SD_OK;
+}
+
+// K and V as one 4-D byte tensor (column box, row, box index, K/V) when V
+// starts a positive multiple of 16 bytes after K: one copy moves a stage's K
+// rows and then its V rows, landing as [K|V][box][row][box bytes] -- what the
+// consumers expect with V box_rows * row_bytes after K. False if the layout
+// or the encoder does not allow it.
+bool encode_kv_map(CUtensorMap* map, void* k, void* v, int row_bytes, int64_t rows, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  const intptr_t dist = reinterpret_cast<intptr_t>(v) - reinterpret_cast<intptr_t>(k);
+  if (!fn || dist <= 0 || dist % 16 != 0 || dist >= (intptr_t(1) << 40)) return false;
+  const int box_bytes = std::min(row_bytes, 128);
+  const int nbox = row_bytes / box_bytes;
+  CUtensorMapSwizzle sw = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : CU_TENSOR_MAP_SWIZZLE_32B;
+  cuuint64_t dims[4] = {cuuint64_t(box_bytes), cuuint64_t(rows), cuuint64_t(nbox), 2};
+  cuuint64_t strides[3] = {cuuint64_t(row_bytes), cuuint64_t(box_bytes), cuuint64_t(dist)};
+  cuuint32_t box[4] = {cuuint32_t(box_bytes), cuuint32_t(box_rows), cuuint32_t(nbox), 2};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, k, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tokens per staged copy for a format (Fmt::kLoadTokens), or 32 when blocks
+// hold 32 tokens.
+int load_tokens(const sd_config& c) {
+  const int lt = (c.kv_bits && elt_size(c.dtype) == 2) ? 64 : sd::kTileTokens;
+  return std::min(lt, c.block_size);
 }
 
 // The four scale/bias arrays of a quantized index (k_scales, k_biases,
@@ -423,6 +454,8 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   cfg.attrs = attr;
   cfg.numAttrs = overlap ? 2 : 1;
   p.sb_fused = x->sb_fused;
+  p.lt = x->lt;
+  p.kv_fused = x->kv_fused;
   p.dbg = x->dbg;
   void* args[4] = {&p, &x->tmK, &x->tmV, &x->tmS};
   SD_CUDA(cudaLaunchKernelExC(&cfg, x->ks.decode, args));
@@ -575,10 +608,15 @@ int32_t sd_index_create(const sd_config* cfg, sd_index** out) {
   // One copy per tile for the four scale/bias pieces: the arena keeps the
   // four arrays sb bytes apart.
   std::memset(&x->tmS, 0, sizeof(x->tmS));
+  x->lt = load_tokens(c);
   x->sb_fused = c.kv_bits && encode_sb_map(&x->tmS, x->k_scales, sb, size_t(BH) * x->cap_local * x->groups * x->esize,
-                                           sd::kTileTokens * x->groups * x->esize) ? 1 : 0;
-  rc = encode_map(&x->tmK, x->k_data, x->row_bytes, BH * x->cap_local);
-  if (rc == SD_OK) rc = encode_map(&x->tmV, x->v_data, x->row_bytes, BH * x->cap_local);
+                                           x->lt * x->groups * x->esize) ? 1 : 0;
+  rc = SD_OK;
+  x->kv_fused = encode_kv_map(&x->tmK, x->k_data, x->v_data, x->row_bytes, BH * x->cap_local, x->lt) ? 1 : 0;
+  if (!x->kv_fused) {
+    rc = encode_map(&x->tmK, x->k_data, x->row_bytes, BH * x->cap_local, x->lt);
+    if (rc == SD_OK) rc = encode_map(&x->tmV, x->v_data, x->row_bytes, BH * x->cap_local, x->lt);
+  }
   if (rc != SD_OK) {
     cudaFree(x->arena);
     delete x;
@@ -962,7 +1000,7 @@ int32_t sd_set_launch_overlap(sd_index* x, int32_t enable) {
 
 #ifdef SD_PHASE_TIMING
 // Phase-timing build only: decode launches of this index write their phase
-// stamps ([grid.y][grid.x][16] u64, see SD_STAMP_* in sd_device.cuh) to buf;
+// stamps ([grid.y][grid.x][24] u64, see SD_STAMP_* in sd_device.cuh) to buf;
 // NULL turns the stamps off.
 int32_t sd_debug_set_phase_buffer(sd_index* x, void* buf) {
   if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
@@ -1143,9 +1181,13 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   x.k_scales = arrays->k_scales; x.k_biases = arrays->k_biases;
   x.v_scales = arrays->v_scales; x.v_biases = arrays->v_biases;
   x.summ = arrays->summaries;
-  rc = encode_map(&x.tmK, x.k_data, x.row_bytes, BH * x.cap_local);
-  if (rc == SD_OK) rc = encode_map(&x.tmV, x.v_data, x.row_bytes, BH * x.cap_local);
-  if (rc != SD_OK) return rc;
+  x.lt = load_tokens(c);
+  x.kv_fused = encode_kv_map(&x.tmK, x.k_data, x.v_data, x.row_bytes, BH * x.cap_local, x.lt) ? 1 : 0;
+  if (!x.kv_fused) {
+    rc = encode_map(&x.tmK, x.k_data, x.row_bytes, BH * x.cap_local, x.lt);
+    if (rc == SD_OK) rc = encode_map(&x.tmV, x.v_data, x.row_bytes, BH * x.cap_local, x.lt);
+    if (rc != SD_OK) return rc;
+  }
 
   sd::DecodeParams p{};
   p.B = c.batch; p.Hq = c.n_q_heads; p.Hkv = c.n_kv_heads; p.S = c.block_size; p.K = c.top_k;
@@ -1190,6 +1232,8 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   lc.attrs = attr;
   lc.numAttrs = 1;
   p.sb_fused = 0;  // the caller's arrays: four 1-D bulk scale/bias copies
+  p.lt = x.lt;
+  p.kv_fused = x.kv_fused;
   void* args[4] = {&p, &x.tmK, &x.tmV, &x.tmS};
   SD_CUDA(cudaLaunchKernelExC(&lc, x.ks.decode, args));
   return SD_OK;

@@ -1,36 +1,47 @@
 // sd_decode.cuh -- the retrieval block-sparse decode kernel for sm_100a.
 //
-// One thread-block cluster of C CTAs serves one (batch, kv-head) group:
-//   phase 0  queries of the group -> shared memory; optional append of the new
+// Q CTAs serve one (batch, kv-head) group: C CTAs of a thread-block cluster
+// times R replica clusters (Q = C * R, all resident at once).
+//   phase 0  queries of the group -> shared memory; the group's summary rows
+//            are bulk-prefetched to L2 and the first register batch of them is
+//            loaded before the query barrier; the producer warp loads the new
 //            token (the cache.update half of attentionWithCacheUpdate,
-//            Libraries/MLXLMCommon/AttentionUtils.swift:54-66 / :67-76). The
-//            first summary loads are issued before the query barrier.
-//   phase 1  score: 8 warps of every CTA score its slice of the candidate
-//            blocks, score[j] = scale * (sum_g q_g) . summary[j], one 16-byte
-//            streaming load of the summary per lane and a fixed fp32
-//            reduction order (the CPU oracle restates it).
-//   phase 2  select: each CTA sorts its candidates in runs of 32 in registers
-//            (bitonic over shuffles) and ranks them by binary search into a
-//            descending top-K list; the lists are exchanged through
-//            distributed shared memory and every candidate's rank in the
-//            group is found the same way; selected = rank < K (ties: lower
-//            block index wins). Result: top-K ascending plus the recent block.
-//   phase 3  attend: the selected blocks are cut into 32-token tiles spread
-//            evenly over the cluster; a producer warp stages K and V tiles
-//            with TMA (128B/64B/32B swizzle, no multicast) into a ring of
+//            Libraries/MLXLMCommon/AttentionUtils.swift:54-66 / :67-76).
+//   phase 1  score: 8 warps score this CTA's candidate rows, score[j] =
+//            scale * (sum_g q_g) . summary[j], one 16-byte load of a summary
+//            row per lane and a fixed fp32 reduction order (the CPU oracle
+//            restates it); meanwhile the producer warp appends the token
+//            (quantizing 4/8-bit rows) and keeps the recent block's running
+//            column sums.
+//   phase 2  select (top-K by score, lower block index wins; then the recent
+//            block), one of two ways:
+//            whole  -- at most 2048 candidates and K <= 128 with clusters of
+//                      several CTAs (or one CTA per group): the cluster's CTAs
+//                      score chunks and push the keys into every peer's copy
+//                      (DSMEM); every CTA runs the same block-wide bitonic
+//                      top-K (replica clusters repeat this);
+//            sliced -- otherwise: CTA q of Q scores chunk q, keeps its best MT
+//                      keys (bucket-histogram threshold), the lists meet in L2
+//                      as epoch-tagged message words, every CTA finds the
+//                      union's K-th key the same way and takes the union's keys
+//                      above it in gathered order; a CTA whose MT keys were all
+//                      taken makes every CTA repeat with full top-K lists.
+//   phase 3  attend: the selected blocks are cut into stages of LT tokens
+//            (64 for 4/8-bit codes with 16-bit scales, else 32) spread evenly
+//            over the group's Q CTAs; a producer warp stages them with TMA
+//            (one 4-D copy for K and V where V lies a fixed stride after K,
+//            one copy for the scale/bias pieces; no multicast) into a ring of
 //            mbarrier-guarded stages; 8 consumer warps run online softmax in
-//            the exp2 domain -- on tensor cores (mma.sync m16n8k16) for
-//            16-bit K/V, on FMA pipes with 4/8-bit codes dequantized in
-//            registers otherwise.
-//   phase 4  merge: warp partials -> CTA partial -> every CTA pushes its
-//            partial to the CTA owning each output slice (DSMEM), one cluster
-//            barrier, log-sum-exp merge from local shared memory.
-// With R > 1 replica clusters per group, every replica scores and selects
-// (cheap, identical results) and attends 1/R of the tiles; the replicas'
-// partials meet in a small global buffer where the last one to arrive at
-// each output slice merges them (no waiting on other clusters).
-// Sharded decode (MODE_CANDIDATES / MODE_ATTEND) runs phases 0-2 and 2-4 as
-// two launches around the caller's all-gather of candidates.
+//            the exp2 domain on tensor cores (mma.sync m16n8k16) for 16-bit
+//            K/V and for 4/8-bit codes with 16-bit scales (exact codes as fp16
+//            operands), on FMA pipes otherwise.
+//   phase 4  merge: warp partials -> CTA partial -> a few owner CTAs each
+//            gather every CTA's record of their output slice (L2 message words
+//            tagged with the group's epoch) and merge them by log-sum-exp; the
+//            other CTAs exit once their records are out.
+// Sharded decode: MODE_PEER exchanges the shards' candidates and partial
+// records through peer memory in the same launch; MODE_CANDIDATES /
+// MODE_ATTEND run phases 0-2 and 2-4 around the caller's all-gathers.
 // Stage-4 semantics follow quantizedScaledDotProductAttention
 // (Libraries/MLXLMCommon/KVCache.swift:1544-1618) restricted to the gathered
 // tokens.
@@ -46,7 +57,7 @@ namespace sd {
 // Ordered stream compaction over [0, n): emit(pos, i) for every i with pred(i),
 // pos ascending with i. All CTA threads call. Returns the number emitted.
 template <class Pred, class Emit>
-__device__ __forceinline__ int cta_compact(int n, Pred pred, Emit emit, int* scratch) {
+__device__ __noinline__ int cta_compact(int n, Pred pred, Emit emit, int* scratch) {
   const int per = (n + blockDim.x - 1) / blockDim.x;
   const int i0 = min(n, int(threadIdx.x) * per), i1 = min(n, i0 + per);
   int cnt = 0;
@@ -493,14 +504,17 @@ __device__ __forceinline__ void consume_tiles_qmma(const DecodeParams& p, const 
         mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
       if (i == warp && warp == 0 && lane == 0) SD_STAMP_HERE(p, 9);
       const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
-      const int nv = min(TS, T - (j * S + tile * TS));
+      const int LT = p.lt;  // the stage holds LT tokens: LT / 32 halves
       uint8_t* stage = tw.ring + s * F::kStageBytes;
-      const uint32_t kb = smem_u32(stage);
-      const uint32_t vb = kb + F::kKvTileBytes;
-      const E* ksc = reinterpret_cast<const E*>(stage + 2 * F::kKvTileBytes);
-      const E* kbi = ksc + TS * NG;
-      const E* vsc = ksc + 2 * TS * NG;
-      const E* vbi = ksc + 3 * TS * NG;
+      for (int hf = 0; hf < LT / TS; ++hf) {
+      const int nv = min(TS, T - (j * S + tile * LT + hf * TS));
+      if (nv <= 0) break;
+      const uint32_t kb = smem_u32(stage) + uint32_t(hf * TS * F::kBoxBytes);
+      const uint32_t vb = smem_u32(stage) + uint32_t(LT * F::kRowBytes + hf * TS * F::kBoxBytes);
+      const E* ksc = reinterpret_cast<const E*>(stage + 2 * LT * F::kRowBytes) + hf * TS * NG;
+      const E* kbi = ksc + LT * NG;
+      const E* vsc = ksc + 2 * LT * NG;
+      const E* vbi = ksc + 3 * LT * NG;
       // --- q.c per group: lane m of the x4 load supplies row r8 of token block mq ---
       float acc[NG][NT][4];
 #pragma unroll
@@ -617,6 +631,7 @@ __device__ __forceinline__ void consume_tiles_qmma(const DecodeParams& p, const 
           }
         }
       }
+      }  // halves of the stage
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(tw.empty + s);
@@ -702,7 +717,10 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     if (BITS != 0 && p.sb_fused) prefetch_tensormap(&tmS);
   }
   const bool owner_recent = ((NB - 1) % P) == pr;
-  const bool appending = p.k_new != nullptr && p.mode != MODE_ATTEND && owner_recent && crank == C - 1;
+  // The new token is appended by the group's last CTA (qrank Q - 1): it attends
+  // the last unit, the recent block's last tile, which holds the new row, and
+  // it keeps the recent block's running column sums.
+  const bool appending = p.k_new != nullptr && p.mode != MODE_ATTEND && owner_recent && qrank == Q - 1;
   // The appended token fills its block: its summary key is written in this
   // launch (from the running column sums).
   const bool completing = p.k_new != nullptr && p.mode != MODE_ATTEND && owner_recent && (T % S) == 0;
@@ -769,7 +787,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   TokenRows<E, BITS, D> tok;
   float rin[EPL];
   const int apos = (T - 1) % S;  // position of the new token in its block
-  const bool keep_sums = appending && rep == 0;
+  const bool keep_sums = appending;
   if (warp == kConsumerWarps && appending) {
     append_load<E, BITS, D>(tok, static_cast<const E*>(p.k_new) + size_t(bh) * D,
                             static_cast<const E*>(p.v_new) + size_t(bh) * D, lane);
@@ -806,9 +824,8 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   // (the producer warp appends the new token meanwhile)
   if (C > 1) cluster_wait();
   if (warp == kConsumerWarps && appending) {
-    // The token's K and V rows; every replica cluster writes them (the same
-    // bytes) so that its own TMA loads are ordered after the write by the
-    // proxy fence here and a barrier of its own before the loads.
+    // The token's K and V rows, ordered before this CTA's own TMA loads of
+    // them by the proxy fence here and a barrier before the loads.
     const size_t row0 = size_t(bh) * p.cap_local + size_t((NB - 1) / P) * S;
     float kdeq[EPL];
     append_store<E, BITS, D>(tok, p.k_data, p.k_scales, p.k_biases, p.v_data, p.v_scales, p.v_biases, row0 + apos,
@@ -816,19 +833,22 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     fence_proxy_async_global();
     // Running column sums of the recent block (fp32, rows in order -- the
     // canonical summary order): acc = acc_before + appended row as stored;
-    // when the appended row fills the block, its summary key is acc / S. One
-    // CTA per group (the appender of replica 0) keeps them.
+    // when the appended row fills the block, its summary key is acc / S.
     if (keep_sums) {
+      // the sums before this row: carried over, or (after a prefill, a load
+      // or a trim of more than one token) summed again from the cache
+      float before[EPL];
+      if (apos > 0 && p.racc_rebuild) {
+        rebuild_sums<E, BITS, D>(p.k_data, p.k_scales, p.k_biases, row0, apos, lane, before);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) before[e] = rin[e];
+      }
 #pragma unroll
       for (int e = 0; e < EPL; ++e) {
         const int d = lane * EPL + e;
         float acc = kdeq[e];
-        if (apos > 0) {
-          const float before = p.racc_rebuild
-                                   ? column_sum<E, BITS, D>(p.k_data, p.k_scales, p.k_biases, row0, apos, d)
-                                   : rin[e];
-          acc = __fadd_rn(before, kdeq[e]);
-        }
+        if (apos > 0) acc = __fadd_rn(before[e], kdeq[e]);
         p.racc_out[size_t(bh) * D + d] = acc;
         if (completing)
           static_cast<E*>(p.summ)[(size_t(bh) * p.nb_stride + (NB - 1) / P) * D + d] =
@@ -848,11 +868,11 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     for (int e = 0; e < EPC; ++e) a = __fmaf_rn(qr[e], f[e], a);
 #pragma unroll
     for (int o = LPB / 2; o >= 1; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+    const float sc = __fmul_rn(a, p.scale);  // every lane of the row's group holds it
+    const uint32_t key = score_key(sc);
+    if (hist_scoring) warp_hist_add(cch == 0 && valid, key >> 20, hbk);
     if (cch == 0 && valid) {
-      const float sc = __fmul_rn(a, p.scale);
-      const uint32_t key = score_key(sc);
       keys[i] = key;
-      if (hist_scoring) atomicAdd(&hbk[key >> 20], 1u);
       if (p.scores_out) p.scores_out[size_t(bh) * NB + size_t(sc0 + i) * P + pr] = sc;
     }
   };
@@ -922,22 +942,47 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     // again over those. The decision depends only on the gathered lists, so
     // every CTA takes the same branch.
     const int MT = p.mt;
-    unsigned long long* lst = reinterpret_cast<unsigned long long*>(sm + L.ring + 144 * 1024);  // <= kMaxTopK
-    int* bidx = reinterpret_cast<int*>(sm + L.ring + 152 * 1024);                              // 2048 ints
-    auto keyf = [&](int i) -> unsigned long long { return full_key(keys[i], jglob(i)); };
-    // this CTA's best m keys, in index order; returns how many. The bucket
-    // histogram of the keys is the one built while scoring the first time.
+    // ring map of this path: [0, 16K) local keys as 64-bit keys (or the u32
+    // keys of a large chunk below 64K) -- later the picks; [64K, 128K) the
+    // gathered lists; [128K, 144K) bucket histogram; [144K, 146K) a bucket's
+    // keys; [146K, 154K) this CTA's list.
+    unsigned long long* lk = reinterpret_cast<unsigned long long*>(sm + L.ring);
+    unsigned long long* g = reinterpret_cast<unsigned long long*>(sm + L.ring + 64 * 1024);
+    unsigned long long* bk = reinterpret_cast<unsigned long long*>(sm + L.ring + 144 * 1024);
+    unsigned long long* lst = reinterpret_cast<unsigned long long*>(sm + L.ring + 146 * 1024);
+    const uint32_t* keys_c = keys;
+    const int cb = c0, Pc = P, prc = pr;
+    auto keyf = [=](int i) -> unsigned long long { return full_key(keys_c[i], (cb + i) * Pc + prc); };
+    const bool small_n = n <= kAllKeysMax;  // the keys live in allk: materialise them as 64-bit keys
+    if (small_n) {
+      for (int i = tid; i < n; i += kThreads) lk[i] = keyf(i);
+      __syncthreads();
+    }
+    SD_STAMP_C(p, 16);
     bool hist_ready = hist_scoring;
-    auto local_list = [&](int m) {
-      if (n > m && m > 0) {
-        const unsigned long long tau = topk_threshold(keyf, n, m, hbk, hist_ready, bidx, 2048, scratch, hist, rs);
+    // this CTA's best m keys into lst, in no particular order; returns how many
+    auto local_list = [&](int m) -> int {
+      if (small_n) {
+        const int c = top_keys(lk, n, m, hbk, hist_ready, lst, bk, scratch, hist, rs);
         hist_ready = false;
-        cta_compact(n, [&](int i) { return keyf(i) >= tau; }, [&](int pos, int i) { lst[pos] = keyf(i); }, scratch);
-      } else {
-        for (int i = tid; i < min(n, m); i += kThreads) lst[i] = keyf(i);
-        __syncthreads();
+        return c;
       }
-      return min(n, m);
+      if (n <= m) {
+        for (int i = tid; i < n; i += kThreads) lst[i] = keyf(i);
+        __syncthreads();
+        return n;
+      }
+      if (m <= 0) return 0;
+      const unsigned long long t =
+          topk_threshold(keyf, n, m, hbk, false, reinterpret_cast<int*>(bk), 512, scratch, hist, rs);
+      if (tid == 0) scratch[119] = 0;
+      __syncthreads();
+      for (int i = tid; i < n; i += kThreads) {
+        const unsigned long long v = keyf(i);
+        if (v >= t) lst[atomicAdd(&scratch[119], 1)] = v;
+      }
+      __syncthreads();
+      return m;
     };
     auto to_pick = [](unsigned long long x) { return make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x)); };
     if (K == 0) {
@@ -947,75 +992,66 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       for (int i = tid; i < kk; i += kThreads) pick[i] = to_pick(lst[i]);
       __syncthreads();
     } else {
-      // publish this CTA's list (0-padded to m key pairs) and gather all Q
-      // lists into g[0, 2*Q*m) (u32 halves of the keys)
-      auto exchange = [&](unsigned long long* area, int m, int nl, uint32_t* g) {
+      // publish this CTA's list (0-padded to m keys; each key as its low and
+      // high 32-bit message words) and gather all Q lists into g[0, Q*m)
+      auto exchange = [&](unsigned long long* area, int m, int nl) {
         unsigned long long* mine = area + size_t(qrank) * m * 2;
         for (int i = tid; i < m; i += kThreads) {
           const unsigned long long x = i < nl ? lst[i] : 0ull;
-          st_msg_gpu(mine + 2 * i, uint32_t(x >> 32), gep);
-          st_msg_gpu(mine + 2 * i + 1, uint32_t(x), gep);
+          st_msg_gpu(mine + 2 * i, uint32_t(x), gep);
+          st_msg_gpu(mine + 2 * i + 1, uint32_t(x >> 32), gep);
         }
-        gather_msgs<false>([&](int i) { return area + i; }, Q * m * 2, gep, kWaitLimitNs, p.err,
+        gather_msgs<false>([area](int i) { return area + i; }, Q * m * 2, gep, kWaitLimitNs, p.err,
                            reinterpret_cast<float*>(g), tid, kThreads, [](int) { return true; });
         __syncthreads();
       };
-      // the union's non-zero keys, compacted into u[] as (score key, block);
-      // tau = its K-th largest key when it holds more than K (else 0: all)
-      unsigned long long tau = 0ull;
-      auto union_topk = [&](const uint32_t* g, int N, uint2* u) {
-        auto gk = [&](int i) { return (static_cast<unsigned long long>(g[2 * i]) << 32) | g[2 * i + 1]; };
-        const int U = cta_compact(N, [&](int i) { return gk(i) != 0ull; },
-                                  [&](int pos, int i) { u[pos] = to_pick(gk(i)); }, scratch);
-        tau = 0ull;
-        if (U > K) {
-          auto ukey = [&](int i) -> unsigned long long { return full_key(u[i].x, int32_t(u[i].y)); };
-          tau = topk_threshold(ukey, U, K, hbk, false, bidx, 2048, scratch, hist, rs);
-        }
-        return U;
-      };
-      uint32_t* g1 = reinterpret_cast<uint32_t*>(sm + L.ring + 64 * 1024);  // 2*Q*MT u32 (<= 32 KB)
-      uint2* u1 = reinterpret_cast<uint2*>(sm + L.ring + 96 * 1024);        // <= Q*MT pairs (<= 32 KB)
       const int nl1 = local_list(MT);
       SD_STAMP_C(p, 15);
-      exchange(p.clist + size_t(bh) * Q * MT * 2, MT, nl1, g1);
+      exchange(p.clist + size_t(bh) * Q * MT * 2, MT, nl1);
       SD_STAMP_C(p, 14);
-      int U = union_topk(g1, Q * MT, u1);
-      uint2* u = u1;
+      int N = Q * MT;
+      int U = hist_keys(g, N, hbk, scratch);
+      SD_STAMP_C(p, 17);
+      unsigned long long tau = U > K ? kth_key(g, N, K, hbk, bk, scratch, hist, rs) : 0ull;
+      SD_STAMP_C(p, 18);
       bool fallback = false;
       if (MT < K) {
         // lists whose CTA had more than MT candidates and whose MT entries are
-        // all selected
-        for (int i = tid; i < Q; i += kThreads) hist[i] = 0u;
-        __syncthreads();
-        for (int i = tid; i < Q * MT; i += kThreads) {
-          const unsigned long long x = (static_cast<unsigned long long>(g1[2 * i]) << 32) | g1[2 * i + 1];
-          if (x != 0ull && x >= tau) atomicAdd(&hist[i / MT], 1u);
-        }
-        __syncthreads();
+        // all selected: the CTA's next key might belong too
+        // (one warp per list: ballots, no shared atomics)
         int need = 0;
-        for (int q = tid; q < Q; q += kThreads) need |= (chunk_lo(q + 1) - chunk_lo(q) > MT && int(hist[q]) == MT);
+        for (int q = warp; q < Q; q += kThreads / 32) {
+          int taken = 0;
+          for (int i = lane; i < MT; i += 32) {
+            const unsigned long long x = g[size_t(q) * MT + i];
+            taken += __popc(__ballot_sync(0xffffffffu, x != 0ull && x >= tau));
+          }
+          if (lane == 0) need |= (chunk_lo(q + 1) - chunk_lo(q) > MT && taken == MT);
+        }
         fallback = __syncthreads_or(need) != 0;
       }
+      SD_STAMP_C(p, 19);
       if (fallback) {
-        uint32_t* g2 = reinterpret_cast<uint32_t*>(sm + L.ring);              // 2*Q*K u32 (<= 64 KB)
-        uint2* u2 = reinterpret_cast<uint2*>(sm + L.ring + 64 * 1024);        // <= Q*K pairs (<= 64 KB)
-        const int nl = local_list(K);  // the keys are intact: they live below 64 KB or in allk
-        exchange(p.cfall + size_t(bh) * Q * K * 2, K, nl, g2);
-        U = union_topk(g2, Q * K, u2);
-        u = u2;
+        // every CTA's full top-K list (the local keys are intact: only the
+        // picks, written below, overwrite them)
+        const int nl = local_list(K);
+        exchange(p.cfall + size_t(bh) * Q * K * 2, K, nl);
+        N = Q * K;
+        U = hist_keys(g, N, hbk, scratch);
+        tau = U > K ? kth_key(g, N, K, hbk, bk, scratch, hist, rs) : 0ull;
       }
       // CANDIDATES mode ends before the group merge, whose owner 0 advances
       // the epoch: CTA 0 holds every list, so every CTA has read the epoch.
       if (p.mode == MODE_CANDIDATES && qrank == 0 && tid == 0) p.gep[bh] = gep;
       kk = min(K, U);
-      if (U > K) {
-        cta_compact(U, [&](int i) { return full_key(u[i].x, int32_t(u[i].y)) >= tau; },
-                    [&](int pos, int i) { pick[pos] = u[i]; }, scratch);
-      } else {
-        for (int i = tid; i < kk; i += kThreads) pick[i] = u[i];
-        __syncthreads();
-      }
+      // the selected keys in the order of the gathered lists: the same order
+      // on every CTA of the group
+      const unsigned long long* gc = g;
+      const unsigned long long tc = tau;
+      uint2* pk = pick;
+      cta_compact(N, [gc, tc](int i) { return gc[i] != 0ull && gc[i] >= tc; },
+                  [gc, pk, to_pick](int pos, int i) { pk[pos] = to_pick(gc[i]); }, scratch);
+      SD_STAMP_C(p, 20);
     }
   }
   // The group's top-K of a candidate union uni[0, U) (score key, block), by
@@ -1170,8 +1206,9 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   }
 
   // ---------------- phase 3: attention over the staged tiles ----------------
-  const int tpb = S / TS;
-  const int recent_tiles = (T - (NB - 1) * S + TS - 1) / TS;
+  const int LT = p.lt;  // tokens per staged copy (a unit of the ring)
+  const int tpb = S / LT;
+  const int recent_tiles = (T - (NB - 1) * S + LT - 1) / LT;
   const int n_units = owner_recent ? (nown - 1) * tpb + recent_tiles : nown * tpb;
   const int u0 = qrank * n_units / Q, u1 = (qrank + 1) * n_units / Q;
   const int nmine = u1 - u0;
@@ -1186,25 +1223,29 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     auto issue = [&](int i) {
       const int s = i % F::kStages;
       const int u = u0 + i, li = u / tpb, tile = u % tpb, j = own[li];
-      const int row = bh * p.cap_local + (j / P) * S + tile * TS;
+      const int row = bh * p.cap_local + (j / P) * S + tile * LT;
       uint8_t* st = sm + L.ring + s * F::kStageBytes;
-      mbar_arrive_expect_tx(full + s, 2 * F::kKvTileBytes + 4 * F::kSbTileBytes);
-      // the tile's K and V, all column boxes of each (two copies: one 4-D copy
-      // of both measured slower at a few tiles per CTA)
-      tma_load_3d(st, &tmK, 0, row, 0, full + s);
-      tma_load_3d(st + F::kKvTileBytes, &tmV, 0, row, 0, full + s);
+      const uint32_t kvb = uint32_t(LT * F::kRowBytes);                        // K (or V) bytes of the stage
+      const uint32_t sbb = F::kQuant ? uint32_t(LT * NG * sizeof(E)) : 0u;     // one scale/bias piece
+      mbar_arrive_expect_tx(full + s, 2 * kvb + 4 * sbb);
+      // the stage's K and V rows, all column boxes: one copy when the K map
+      // covers V too (4-D, V one fixed stride after K), else one each
+      if (p.kv_fused) {
+        tma_load_4d(st, &tmK, 0, row, 0, 0, full + s);
+      } else {
+        tma_load_3d(st, &tmK, 0, row, 0, full + s);
+        tma_load_3d(st + kvb, &tmV, 0, row, 0, full + s);
+      }
       if constexpr (BITS != 0) {
         const size_t so = size_t(row) * NG * sizeof(E);
-        uint8_t* sb = st + 2 * F::kKvTileBytes;
+        uint8_t* sb = st + 2 * kvb;
         if (p.sb_fused) {
           tma_load_2d(sb, &tmS, int32_t(so), 0, full + s);  // so < 2^31 whenever the map is used
         } else {
-          bulk_load(sb, static_cast<const uint8_t*>(p.k_scales) + so, F::kSbTileBytes, full + s);
-          bulk_load(sb + F::kSbTileBytes, static_cast<const uint8_t*>(p.k_biases) + so, F::kSbTileBytes, full + s);
-          bulk_load(sb + 2 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_scales) + so, F::kSbTileBytes,
-                    full + s);
-          bulk_load(sb + 3 * F::kSbTileBytes, static_cast<const uint8_t*>(p.v_biases) + so, F::kSbTileBytes,
-                    full + s);
+          bulk_load(sb, static_cast<const uint8_t*>(p.k_scales) + so, sbb, full + s);
+          bulk_load(sb + sbb, static_cast<const uint8_t*>(p.k_biases) + so, sbb, full + s);
+          bulk_load(sb + 2 * sbb, static_cast<const uint8_t*>(p.v_scales) + so, sbb, full + s);
+          bulk_load(sb + 3 * sbb, static_cast<const uint8_t*>(p.v_biases) + so, sbb, full + s);
         }
       }
       *issued = i + 1;

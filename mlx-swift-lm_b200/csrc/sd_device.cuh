@@ -127,22 +127,24 @@ __device__ __forceinline__ uint64_t globaltimer() {
 }
 
 // Phase stamps of the decode kernel, compiled only into the phase-timing
-// build (-DSD_PHASE_TIMING): 16 u64 per CTA in DecodeParams::dbg. Thread 0
+// build (-DSD_PHASE_TIMING): 24 u64 per CTA in DecodeParams::dbg. Thread 0
 // writes [0] %globaltimer at entry and [7] at exit, and clock64 at [1] entry,
 // [2] scoring start, [3] scoring end, [4] selection end, [5] attention end,
 // [6] merge end; [14]/[15] inside the selection (the local list / the
 // exchange). One thread of the producer warp writes [8] (first ring fill
 // issued), consumer warp 0's lane 0 [9] (its first tile arrived) and [10]
 // (its last tile done), thread 0 [11] (partials written), [12] (merge
-// records stored) and [13] (merge records gathered). The product build has
-// no stamps.
+// records stored) and [13] (merge records gathered); in the sliced
+// selection thread 0 writes [16] (64-bit keys built), [17] (union
+// histogram), [18] (union threshold), [19] (list check) and [20] (picks).
+// The product build has no stamps.
 #ifdef SD_PHASE_TIMING
 __device__ __forceinline__ unsigned long long clock_u64() {
   unsigned long long c;
   asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
   return c;
 }
-#define SD_DBG_SLOT(p, k) (p).dbg[(size_t(blockIdx.y) * gridDim.x + blockIdx.x) * 16 + (k)]
+#define SD_DBG_SLOT(p, k) (p).dbg[(size_t(blockIdx.y) * gridDim.x + blockIdx.x) * 24 + (k)]
 #define SD_STAMP_T(p, k)                                             \
   do {                                                               \
     if (threadIdx.x == 0 && (p).dbg) SD_DBG_SLOT(p, k) = ::sd::globaltimer(); \
@@ -246,7 +248,7 @@ __device__ __forceinline__ uint32_t ld_msg(const unsigned long long* p, uint32_t
 // kSys: the words are written by other GPUs (system scope) rather than by
 // other CTAs of this GPU.
 template <bool kSys, class Addr, class Want>
-__device__ __forceinline__ void gather_msgs(Addr addr, int n, uint32_t epoch, uint64_t limit_ns, int* err, float* dst,
+__device__ __noinline__ void gather_msgs(Addr addr, int n, uint32_t epoch, uint64_t limit_ns, int* err, float* dst,
                                             int tid, int nthreads, Want want) {
   constexpr int BATCH = 8;
   for (int base = tid; base < n; base += nthreads * BATCH) {
@@ -324,6 +326,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                            int32_t w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
       : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
@@ -644,7 +654,7 @@ struct RadixState {
 // i.e. the k largest keys. Requires 0 < k < n. All CTA threads call it.
 // hist: 256 u32 of shared memory.
 template <class KeyF>
-__device__ void radix_select(KeyF keyf, int n, int k, uint32_t* hist, RadixState* st) {
+__device__ __noinline__ void radix_select(KeyF keyf, int n, int k, uint32_t* hist, RadixState* st) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
   unsigned long long prefix = 0ull, mask = 0ull;
   int rem = k;
@@ -722,7 +732,7 @@ __device__ __forceinline__ uint32_t key_bucket(unsigned long long x) { return ui
 // (equal scores, say) a radix select over all n keys decides instead. All CTA
 // threads call; scratch: cta_exclusive_scan's 33 ints plus [120, 124).
 template <class KeyF>
-__device__ unsigned long long topk_threshold(KeyF keyf, int n, int k, uint32_t* h, bool have_hist, int* bidx,
+__device__ __noinline__ unsigned long long topk_threshold(KeyF keyf, int n, int k, uint32_t* h, bool have_hist, int* bidx,
                                              int cap, int* scratch, uint32_t* hist256, RadixState* rs) {
   const int tid = threadIdx.x, nthr = blockDim.x;
   unsigned long long* tau = reinterpret_cast<unsigned long long*>(scratch + 122);
@@ -784,6 +794,151 @@ __device__ unsigned long long topk_threshold(KeyF keyf, int n, int k, uint32_t* 
   const unsigned long long t = *tau;
   __syncthreads();
   return t;
+}
+
+// ---------------------------------------------------------------------------
+// Top-K building blocks over 64-bit keys in shared memory (the sliced
+// selection): keys are distinct, 0 marks padding. All CTA threads call each
+// function; scratch: cta_exclusive_scan's 33 ints, [118, 124).
+// ---------------------------------------------------------------------------
+
+// Shared-memory atomics aimed at one address serialise across a warp, so the
+// selection aggregates them per warp. warp_slot: a slot in a buffer with
+// counter *ctr for every lane whose `want` holds (one atomic per warp); all
+// lanes of the warp call it.
+__device__ __forceinline__ int warp_slot(bool want, int* ctr) {
+  const unsigned m = __ballot_sync(0xffffffffu, want);
+  const int lane = threadIdx.x & 31;
+  int base = 0;
+  if (m && lane == __ffs(m) - 1) base = atomicAdd(ctr, __popc(m));
+  base = __shfl_sync(0xffffffffu, base, __ffs(m ? m : 1u) - 1);
+  return base + __popc(m & ((1u << lane) - 1u));
+}
+// h[bucket] += 1 for every lane whose `want` holds, one atomic per distinct
+// bucket of the warp; all lanes of the warp call it.
+__device__ __forceinline__ void warp_hist_add(bool want, uint32_t bucket, uint32_t* h) {
+  const unsigned m = __ballot_sync(0xffffffffu, want);
+  if (want) {
+    const unsigned peers = __match_any_sync(m, bucket);
+    if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&h[bucket], uint32_t(__popc(peers)));
+  }
+}
+
+// Bucket histogram of the non-zero keys x[0, n); returns their number.
+static __device__ __noinline__ int hist_keys(const unsigned long long* x, int n, uint32_t* h, int* scratch) {
+  for (int i = threadIdx.x; i < kBuckets; i += blockDim.x) h[i] = 0u;
+  if (threadIdx.x == 0) scratch[118] = 0;
+  __syncthreads();
+  int c = 0;
+  for (int b0 = threadIdx.x & ~31; b0 < n; b0 += blockDim.x) {  // whole warps in step
+    const int i = b0 + (threadIdx.x & 31);
+    const unsigned long long v = i < n ? x[i] : 0ull;
+    warp_hist_add(v != 0ull, key_bucket(v), h);
+    c += v != 0ull ? 1 : 0;
+  }
+  c = __reduce_add_sync(0xffffffffu, c);
+  if ((threadIdx.x & 31) == 0 && c) atomicAdd(&scratch[118], c);
+  __syncthreads();
+  const int total = scratch[118];
+  __syncthreads();
+  return total;
+}
+
+// The k-th largest non-zero key of x[0, n) (1 <= k <= number of non-zero
+// keys), h being the bucket histogram of x: the bucket holding it is found
+// from h; that bucket's keys (usually a few dozen) are gathered into bk (256
+// entries) and ranked by counting. A bucket of more than 256 keys (equal
+// scores) is resolved by a radix select over x instead.
+static __device__ __noinline__ unsigned long long kth_key(const unsigned long long* x, int n, int k, const uint32_t* h,
+                                                   unsigned long long* bk, int* scratch, uint32_t* hist256,
+                                                   RadixState* rs) {
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  unsigned long long* tau = reinterpret_cast<unsigned long long*>(scratch + 122);
+  const int per = (kBuckets + nthr - 1) / nthr;
+  const int top = kBuckets - 1 - tid * per;
+  int cnt = 0;
+  for (int j = 0; j < per; ++j)
+    if (top - j >= 0) cnt += int(h[top - j]);
+  int total;
+  const int before = cta_exclusive_scan(cnt, scratch, &total);
+  if (before < k && before + cnt >= k) {
+    int acc = before;
+    for (int j = 0; j < per && top - j >= 0; ++j) {
+      const int c = int(h[top - j]);
+      if (acc + c >= k) {
+        scratch[120] = top - j;
+        scratch[121] = acc;
+        break;
+      }
+      acc += c;
+    }
+  }
+  if (tid == 0) {
+    *tau = ~0ull;
+    scratch[119] = 0;
+  }
+  __syncthreads();
+  const uint32_t b = uint32_t(scratch[120]);
+  const int r = k - scratch[121];  // keys still needed from bucket b (>= 1)
+  const int nb = int(h[b]);
+  if (nb <= 256) {
+    for (int b0 = tid & ~31; b0 < n; b0 += nthr) {
+      const int i = b0 + (tid & 31);
+      const unsigned long long v = i < n ? x[i] : 0ull;
+      const bool in = v != 0ull && key_bucket(v) == b;
+      const int slot = warp_slot(in, &scratch[119]);
+      if (in) bk[slot] = v;
+    }
+    __syncthreads();
+    for (int a = tid; a < nb; a += nthr) {
+      const unsigned long long v = bk[a];
+      int rank = 0;
+#pragma unroll 8
+      for (int c = 0; c < nb; ++c) rank += bk[c] > v ? 1 : 0;  // the same word for every thread: broadcast
+      if (rank == r - 1) *tau = v;
+    }
+  } else {
+    radix_select([x](int i) { return x[i]; }, n, k, hist256, rs);
+    const unsigned long long pre = rs->prefix, msk = rs->mask;
+    unsigned long long m = ~0ull;
+    for (int i = tid; i < n; i += nthr) {
+      const unsigned long long v = x[i];
+      if (v && (v & msk) >= pre && v < m) m = v;
+    }
+    atomicMin(tau, m);
+  }
+  __syncthreads();
+  const unsigned long long t = *tau;
+  __syncthreads();
+  return t;
+}
+
+// The m largest keys of the distinct non-zero keys x[0, n) into out, in no
+// particular order; returns min(n, m). h: the bucket histogram of x when
+// have_hist (it is built here otherwise).
+static __device__ __noinline__ int top_keys(const unsigned long long* x, int n, int m, uint32_t* h, bool have_hist,
+                                     unsigned long long* out, unsigned long long* bk, int* scratch,
+                                     uint32_t* hist256, RadixState* rs) {
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  if (n <= m) {
+    for (int i = tid; i < n; i += nthr) out[i] = x[i];
+    __syncthreads();
+    return n;
+  }
+  if (m <= 0) return 0;
+  if (!have_hist) hist_keys(x, n, h, scratch);
+  const unsigned long long t = kth_key(x, n, m, h, bk, scratch, hist256, rs);
+  if (tid == 0) scratch[119] = 0;
+  __syncthreads();
+  for (int b0 = tid & ~31; b0 < n; b0 += nthr) {
+    const int i = b0 + (tid & 31);
+    const unsigned long long v = i < n ? x[i] : 0ull;
+    const bool in = i < n && v >= t;
+    const int slot = warp_slot(in, &scratch[119]);
+    if (in) out[slot] = v;
+  }
+  __syncthreads();
+  return m;
 }
 
 }  // namespace sd

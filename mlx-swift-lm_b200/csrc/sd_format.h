@@ -35,8 +35,14 @@ struct Fmt {
   static constexpr int kNChunk = kRowBytes / 16;       // chunks per row
   static constexpr int kEpc = 128 / kEltBits;          // elements per 16-byte chunk
   static constexpr int kGroups = kQuant ? D / 64 : 1;  // quantization groups per row
-  static constexpr int kKvTileBytes = kTileTokens * kRowBytes;
-  static constexpr int kSbTileBytes = kQuant ? kTileTokens * kGroups * ESIZE : 0;
+  // Token rows of one staged copy (the TMA box): 64 for 4/8-bit codes with
+  // 16-bit scales, whose tensor-core consumer walks a stage as two 32-token
+  // halves (fewer, larger copies: the TMA unit's per-copy cost dominates
+  // tiles of a few KB); 32 otherwise. Blocks of 32 tokens stage 32 (the
+  // host picks the box; the stage is sized for kLoadTokens).
+  static constexpr int kLoadTokens = (kQuant && ESIZE == 2) ? 64 : kTileTokens;
+  static constexpr int kKvTileBytes = kLoadTokens * kRowBytes;
+  static constexpr int kSbTileBytes = kQuant ? kLoadTokens * kGroups * ESIZE : 0;
   static constexpr int kStageBytes = align_up(2 * kKvTileBytes + 4 * kSbTileBytes, 1024);
   static constexpr int kStages = (kRingBytes / kStageBytes) < 16 ? (kRingBytes / kStageBytes) : 16;
   // PV mapping: each lane owns kPiece bytes (kDpl dims) of a row; kRpp rows per pass.

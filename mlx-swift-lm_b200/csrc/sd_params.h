@@ -64,7 +64,11 @@ struct DecodeParams {
   // v_scales, v_biases at one fixed stride), one copy per tile. 0: four 1-D
   // bulk copies.
   int sb_fused;
-  unsigned long long* dbg;  // phase-timing build only: [grid.y][grid.x][16] stamps, or null
+  // Tokens per staged copy (Fmt::kLoadTokens, or 32 for blocks of 32 tokens),
+  // and 1 when the K tensor map covers V too (one copy per stage for both).
+  int lt;
+  int kv_fused;
+  unsigned long long* dbg;  // phase-timing build only: [grid.y][grid.x][24] stamps, or null
 };
 
 struct AppendParams {

@@ -126,6 +126,15 @@ __device__ __forceinline__ float column_sum(const void* data, const void* scales
   return acc;
 }
 
+// Column sums of the lane's D/32 columns over n rows from `row0` (the
+// canonical order of column_sum) into out -- the rare rebuild of a decode
+// step's running sums, kept out of line.
+template <typename E, int BITS, int D>
+__device__ __noinline__ void rebuild_sums(const void* data, const void* scales, const void* biases, size_t row0,
+                                          int n, int lane, float* out) {
+  for (int e = 0; e < D / 32; ++e) out[e] = column_sum<E, BITS, D>(data, scales, biases, row0, n, lane * (D / 32) + e);
+}
+
 // Write one token row of K and V (warp 0: K, warp 1: V) at local row `row`.
 template <typename E, int BITS, int D>
 __device__ __forceinline__ void write_token_row(const E* src, void* data, void* scales, void* biases,

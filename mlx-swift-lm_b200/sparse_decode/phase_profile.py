@@ -31,7 +31,10 @@ PHASES = ["prologue", "score", "select", "attend", "merge"]
 SUBPHASES = [("select.local_or_cluster_wait", 3, 15), ("select.exchange_or_topk", 15, 14), ("select.rest", 14, 4),
              ("attend.first_fill_issued", 4, 8), ("attend.warp0_first_tile", 4, 9), ("attend.warp0_tiles", 9, 10),
              ("attend.tail", 10, 5), ("merge.cta_partial", 5, 11), ("merge.store", 11, 12),
-             ("merge.gather", 12, 13), ("merge.output", 13, 6)]
+             ("merge.gather", 12, 13), ("merge.output", 13, 6),
+             ("sliced.keys64", 3, 16), ("sliced.local_list", 16, 15), ("sliced.union_hist", 14, 17),
+             ("sliced.union_kth", 17, 18), ("sliced.list_check", 18, 19), ("sliced.picks", 19, 20),
+             ("sliced.after_picks", 20, 4)]
 
 
 def _load_phase_lib():
@@ -69,7 +72,7 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True) -> 
         idx.set_launch_overlap(overlap)
         gx, gy = ctypes.c_int32(), ctypes.c_int32()
         _check(L.sd_debug_grid(idx._h, ctypes.byref(gx), ctypes.byref(gy)))
-        buf = torch.zeros((gy.value, gx.value, 16), dtype=torch.int64, device="cuda")
+        buf = torch.zeros((gy.value, gx.value, 24), dtype=torch.int64, device="cuda")
         _check(L.sd_debug_set_phase_buffer(idx._h, ctypes.c_void_p(buf.data_ptr())))
         items.append({"idx": idx, "q": case["q"].contiguous(), "k": k[:, :, w.T - 1].contiguous(),
                       "v": v[:, :, w.T - 1].contiguous(), "out": torch.empty_like(case["q"]), "buf": buf})
@@ -102,7 +105,7 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True) -> 
     per_sub = {n: [] for n, _, _ in SUBPHASES}
     spans, entries, exits, skews = [], [], [], []
     for it in items:
-        a = it["buf"].cpu().reshape(-1, 16).tolist()
+        a = it["buf"].cpu().reshape(-1, 24).tolist()
         ph = {p: [] for p in PHASES}
         sub = {n: [] for n, _, _ in SUBPHASES}
         for r in a:
