@@ -288,7 +288,7 @@ def run_reference(args, w, rank: int, world: int) -> None:
             "warmup": args.warmup, "ms_per_step": round(v * w.layers / 1000, 4), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
             "data": "synthetic (seeded N(0,1) Q/K/V, planted needle blocks)", "impl": "reference",
-            "config": _config(w),
+            "config": _config(w, world, gpu=False),
             "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": used, "kind": "port",
                              "sample": f"one layer per repetition ({w.name}), median of {args.steps} samples of "
                                        f"~{per:.0f}s after {setup_s:.0f}s of input set-up; the reference (Swift + "
@@ -298,16 +298,19 @@ def run_reference(args, w, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def _config(w, world: int = 1) -> dict:
+def _config(w, world: int = 1, gpu: bool = True) -> dict:
+    """The workload keys (both arms) plus, for the GPU arm, how it ran."""
     from sparse_decode.synth import algorithmic_bytes
     b = algorithmic_bytes(w)
-    return {"workload": w.name, "batch": w.B, "q_heads": w.Hq, "kv_heads": w.Hkv, "head_dim": w.D,
-            "context": w.T, "block": w.S, "top_k": w.K, "kv_bits": w.bits, "layers_per_step": w.layers,
-            "parallelism": f"sequence-sharded x{world} (fused peer-memory exchange)" if world > 1 else "single GPU",
-            "l2": f"inputs larger than L2 ({w.layers} layers x {b / 1e6:.1f} MB per step)"
-                  if w.layers * b > 126e6 else
-                  f"inputs smaller than L2 ({w.layers} layers x {b / 1e6:.1f} MB): not a bench line",
-            "cuda_graph": True}
+    c = {"workload": w.name, "batch": w.B, "q_heads": w.Hq, "kv_heads": w.Hkv, "head_dim": w.D,
+         "context": w.T, "block": w.S, "top_k": w.K, "kv_bits": w.bits, "layers_per_step": w.layers}
+    if gpu:
+        c["parallelism"] = f"sequence-sharded x{world} (fused peer-memory exchange)" if world > 1 else "single GPU"
+        c["l2"] = (f"inputs larger than L2 ({w.layers} layers x {b / 1e6:.1f} MB per step)"
+                   if w.layers * b > 126e6 else
+                   f"inputs smaller than L2 ({w.layers} layers x {b / 1e6:.1f} MB): not a bench line")
+        c["cuda_graph"] = True
+    return c
 
 
 def _rel_err(a, b) -> float:

@@ -128,6 +128,7 @@ struct sd_index {
   sd::KernelSet ks;
   bool attrs_set;
   unsigned long long* dbg;  // phase-timing build: stamp buffer of the decode launches
+  int l2_plain;  // phase-timing build: 1 drops the L2 evict_first hint (comparison runs)
 };
 
 // Exchange area of one shard for the fused sharded step (sd_shard_decode);
@@ -137,7 +138,8 @@ struct sd_comm {
   int P, pr, BH, K, C, R, G, D, RS;
   int resident;                     // every cluster of a launch fits on the GPU at once
   size_t bytes;
-  int64_t off_cand, off_part, off_ctl;
+  int64_t off_cand, off_part, off_ctl, off_clst;
+  int MP;                           // sliced selection: keys per CTA list across the shards (0: unused)
   uint8_t* local;
   uint8_t* peers[sd::kMaxShards];   // own area at [pr]
   bool opened;
@@ -265,11 +267,13 @@ int max_active_clusters(const sd_index* x, int C) {
   return n;
 }
 
-// Candidate blocks of this shard when the cache is full.
+// Candidate blocks of the largest shard (rank 0) when the cache is full: the
+// same on every shard, so every shard of a sequence picks the same launch
+// shape and selection path.
 int64_t max_local_candidates(const sd_index* x) {
   const sd_config& c = x->cfg;
   const int64_t ncand = x->nb_global - 1;
-  return ncand > c.shard_rank ? (ncand - c.shard_rank + c.shard_count - 1) / c.shard_count : 0;
+  return ncand > 0 ? (ncand + c.shard_count - 1) / c.shard_count : 0;
 }
 
 // Whether a launch with nloc candidate blocks per group takes the sliced
@@ -422,6 +426,8 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   if (mode == sd::MODE_PEER) {
     for (int r = 0; r < comm->P; ++r) p.peer[r] = comm->peers[r];
     p.x_cand = comm->off_cand;
+    p.x_clst = comm->off_clst;
+    p.mtp = comm->MP;
     p.x_part = comm->off_part;
     p.x_ctl = comm->off_ctl;
     p.peer_wait_ns = comm->wait_ns;
@@ -429,6 +435,13 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   const int64_t ncand = p.NB - 1;
   const int64_t nloc = ncand > p.pr ? (ncand - p.pr + p.P - 1) / p.P : 0;
   p.sliced = sliced_launch(x, nloc) ? 1 : 0;
+  // The one-level exchange across the shards needs every shard on the sliced
+  // path: the shard with the fewest candidates (the last) decides, the same
+  // answer on every shard.
+  if (mode == sd::MODE_PEER) {
+    const int64_t nmin = ncand > p.P - 1 ? (ncand - (p.P - 1) + p.P - 1) / p.P : 0;
+    if (!sliced_launch(x, nmin)) p.mtp = 0;
+  }
   const int64_t chunks = p.sliced ? int64_t(x->C) * x->R : x->C;
   if ((nloc + chunks - 1) / chunks > sd::kLocalKeysMax)
     return fail(SD_ERR_SHAPE, "too many blocks per CTA (%lld) for %lld CTAs per group",
@@ -457,6 +470,7 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   p.lt = x->lt;
   p.kv_fused = x->kv_fused;
   p.dbg = x->dbg;
+  p.l2_plain = x->l2_plain;
   void* args[4] = {&p, &x->tmK, &x->tmV, &x->tmS};
   SD_CUDA(cudaLaunchKernelExC(&cfg, x->ks.decode, args));
   return SD_OK;
@@ -848,9 +862,19 @@ int32_t sd_comm_create(const sd_index* x, sd_comm** out) {
   m.RS = merge_record(Q, m.G, m.D);
   m.resident = max_active_clusters(x, x->C) >= int64_t(m.BH) * x->R ? 1 : 0;
   const int64_t P = m.P, BH = m.BH;
+  // one-level selection across the shards (indexes that slice): lists of MP
+  // keys, about four times a CTA's share of the top-K, P * Q * MP <= 8192
+  m.MP = 0;
+  if (c.top_k > 0 && (c.top_k > 128 || max_local_candidates(x) > sd::kAllKeysMax || (m.C == 1 && m.R > 1))) {
+    int mp = 4 * ((c.top_k + int(P) * Q - 1) / (int(P) * Q));
+    mp = std::min(std::max(32, (mp + 31) / 32 * 32), c.top_k);
+    mp = std::min(mp, 8192 / (int(P) * Q));
+    m.MP = mp >= 1 ? mp : 0;
+  }
   m.off_cand = 0;
   m.off_part = m.off_cand + int64_t(align256(size_t(P * BH * std::max(m.K, 1) * 2 * 8)));
-  m.off_ctl = m.off_part + int64_t(align256(size_t(P * BH * NO * m.RS * 8)));
+  m.off_clst = m.off_part + int64_t(align256(size_t(P * BH * NO * m.RS * 8)));
+  m.off_ctl = m.off_clst + int64_t(align256(size_t(P * BH * Q * std::max(m.MP, 1) * 2 * 8)));
   m.bytes = size_t(m.off_ctl) + 256;
   int dev = 0;
   SD_CUDA(cudaGetDevice(&dev));
@@ -1005,6 +1029,11 @@ int32_t sd_set_launch_overlap(sd_index* x, int32_t enable) {
 int32_t sd_debug_set_phase_buffer(sd_index* x, void* buf) {
   if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
   x->dbg = static_cast<unsigned long long*>(buf);
+  return SD_OK;
+}
+int32_t sd_debug_set_l2_plain(sd_index* x, int32_t plain) {
+  if (!x) return fail(SD_ERR_INVALID_ARG, "NULL index");
+  x->l2_plain = plain ? 1 : 0;
   return SD_OK;
 }
 int32_t sd_debug_grid(const sd_index* x, int32_t* grid_x, int32_t* grid_y) {

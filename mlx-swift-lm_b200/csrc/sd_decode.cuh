@@ -61,9 +61,11 @@ __device__ __noinline__ int cta_compact(int n, Pred pred, Emit emit, int* scratc
   const int per = (n + blockDim.x - 1) / blockDim.x;
   const int i0 = min(n, int(threadIdx.x) * per), i1 = min(n, i0 + per);
   int cnt = 0;
+#pragma unroll 1
   for (int i = i0; i < i1; ++i) cnt += pred(i) ? 1 : 0;
   int total;
   int pos = cta_exclusive_scan(cnt, scratch, &total);
+#pragma unroll 1
   for (int i = i0; i < i1; ++i)
     if (pred(i)) emit(pos++, i);
   __syncthreads();
@@ -503,6 +505,7 @@ __device__ __forceinline__ void consume_tiles_qmma(const DecodeParams& p, const 
     if ((i < F::kStages || wait_issued(tw.issued, i, p.err)) &&
         mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
       if (i == warp && warp == 0 && lane == 0) SD_STAMP_HERE(p, 9);
+      if (i == warp + kConsumerWarps && warp == 0 && lane == 0) SD_STAMP_HERE(p, 23);
       const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
       const int LT = p.lt;  // the stage holds LT tokens: LT / 32 halves
       uint8_t* stage = tw.ring + s * F::kStageBytes;
@@ -753,6 +756,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   const int sub = lane / LPB, cch = lane % LPB;
   const bool scorer = warp < NWS && p.mode != MODE_ATTEND;
   const uint8_t* sbase = static_cast<const uint8_t*>(p.summ) + (size_t(bh) * p.nb_stride + sc0) * D * sizeof(E);
+  const uint64_t spol = stream_policy(p.l2_plain != 0);  // L2 policy of the streamed summaries and K/V tiles
   // The CTA's summary rows go to L2 at once: one bulk prefetch per 64 KB
   // (thread 0; safe before the grid-dependency wait -- L2 is coherent and a
   // prefetch never returns data), so the register batches below stream from
@@ -760,23 +764,36 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   if (p.mode != MODE_ATTEND && tid == 0 && sn > 0) {
     constexpr int SROW = D * int(sizeof(E));
     for (size_t off = 0; off < size_t(sn) * SROW; off += 65536)
-      bulk_prefetch_l2(sbase + off, uint32_t(min(size_t(65536), size_t(sn) * SROW - off)));
+      bulk_prefetch_l2(sbase + off, uint32_t(min(size_t(65536), size_t(sn) * SROW - off)), spol);
   }
-  // Sliced selection with the keys in allk: the histogram of the keys'
-  // buckets that the top-K threshold search (topk_threshold) needs is built
-  // while scoring, in the ring.
+  // bucket histogram of the sliced selection's threshold searches (in the ring)
   uint32_t* hbk = reinterpret_cast<uint32_t*>(sm + L.ring + 128 * 1024);
-  const bool hist_scoring = !whole && K > 0 && keys != reinterpret_cast<uint32_t*>(sm + L.ring) &&
-                            p.mode != MODE_ATTEND;
-  if (hist_scoring)
-    for (int i = tid; i < kBuckets; i += kThreads) hbk[i] = 0u;
   const uint8_t* srow0 = sbase + cch * 16;
+  // Lane-staged scoring (the keys do not live in the ring): every lane copies
+  // its own 16-byte chunks of NBQ batches ahead into a slot of the ring with
+  // cp.async (128 KB in flight per CTA instead of a register batch), and
+  // reads back only what it copied itself -- no waits between lanes.
+  constexpr int NBQ = 4;                                 // batches in flight per warp
+  constexpr int BATCH_ROWS = NWS * BPW * UNR;            // rows of one batch of the CTA
+  const bool lstage = p.mode != MODE_ATTEND && keys != reinterpret_cast<uint32_t*>(sm + L.ring);
+  const uint32_t lslot = smem_u32(sm + L.ring) + uint32_t(warp * NBQ * UNR * 512 + lane * 16);
+  auto stage_batch = [&](int bt) {  // batch bt of this warp into slot bt % NBQ, one commit group
+    const int it = warp * BPW + bt * BATCH_ROWS;
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const int i = it + u * NWS * BPW + sub;
+      if (i < sn) cp_async16(lslot + uint32_t(((bt % NBQ) * UNR + u) * 512), srow0 + size_t(i) * D * sizeof(E), spol);
+    }
+    cp_async_commit();
+  };
   uint4 raw[UNR];
-  if (scorer) {
+  if (scorer && lstage) {
+    for (int bt = 0; bt < NBQ; ++bt) stage_batch(bt);
+  } else if (scorer) {
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
       const int i = warp * BPW + u * NWS * BPW + sub;
-      raw[u] = i < sn ? ldg_stream(srow0 + size_t(i) * D * sizeof(E)) : make_uint4(0u, 0u, 0u, 0u);
+      raw[u] = i < sn ? ldg_stream(srow0 + size_t(i) * D * sizeof(E), spol) : make_uint4(0u, 0u, 0u, 0u);
     }
   }
 
@@ -868,15 +885,28 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     for (int e = 0; e < EPC; ++e) a = __fmaf_rn(qr[e], f[e], a);
 #pragma unroll
     for (int o = LPB / 2; o >= 1; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-    const float sc = __fmul_rn(a, p.scale);  // every lane of the row's group holds it
-    const uint32_t key = score_key(sc);
-    if (hist_scoring) warp_hist_add(cch == 0 && valid, key >> 20, hbk);
     if (cch == 0 && valid) {
-      keys[i] = key;
+      const float sc = __fmul_rn(a, p.scale);
+      keys[i] = score_key(sc);
       if (p.scores_out) p.scores_out[size_t(bh) * NB + size_t(sc0 + i) * P + pr] = sc;
     }
   };
-  if (scorer) {
+  if (scorer && lstage) {
+    float qr[EPC];
+#pragma unroll
+    for (int e = 0; e < EPC; ++e) qr[e] = qsum[cch * EPC + e];
+    for (int bt = 0, it = warp * BPW; it < sn; ++bt, it += BATCH_ROWS) {
+      cp_async_wait<NBQ - 1>();  // this lane's copies of batch bt have landed
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int i = it + u * NWS * BPW + sub;
+        const uint4 v = lds128(lslot + uint32_t(((bt % NBQ) * UNR + u) * 512));
+        score_row(v, qr, i, i < sn);
+      }
+      stage_batch(bt + NBQ);  // into the slot just read (this lane's own chunks)
+    }
+    cp_async_wait<0>();
+  } else if (scorer) {
     float qr[EPC];
 #pragma unroll
     for (int e = 0; e < EPC; ++e) qr[e] = qsum[cch * EPC + e];
@@ -889,7 +919,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
 #pragma unroll
         for (int u = 0; u < UNR; ++u) {
           const int i = nx + u * NWS * BPW + sub;
-          raw[u] = i < sn ? ldg_stream(srow0 + size_t(i) * D * sizeof(E)) : make_uint4(0u, 0u, 0u, 0u);
+          raw[u] = i < sn ? ldg_stream(srow0 + size_t(i) * D * sizeof(E), spol) : make_uint4(0u, 0u, 0u, 0u);
         }
       }
 #pragma unroll
@@ -912,6 +942,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   // ---------------- phase 2: selection ----------------
   SD_STAMP_C(p, 3);
   int kk;  // blocks chosen by top-K
+  bool global_done = false;  // peer mode: pick[0, kk) is already the top-K of every shard
   if (whole) {
     if (C > 1) cluster_sync();  // every peer's pushed keys have landed
     SD_STAMP_C(p, 15);
@@ -959,7 +990,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       __syncthreads();
     }
     SD_STAMP_C(p, 16);
-    bool hist_ready = hist_scoring;
+    bool hist_ready = false;
     // this CTA's best m keys into lst, in no particular order; returns how many
     auto local_list = [&](int m) -> int {
       if (small_n) {
@@ -985,7 +1016,56 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       return m;
     };
     auto to_pick = [](unsigned long long x) { return make_uint2(uint32_t(x >> 32), 0xffffffffu - uint32_t(x)); };
-    if (K == 0) {
+    if (peer && K > 0 && p.mtp > 0) {
+      // One level across the shards: this CTA's best MP keys go to every
+      // shard's exchange area (message words tagged with the launch epoch);
+      // every CTA of every shard gathers the group's P x Q lists from its own
+      // area and takes the top-K of their union -- the same set in the same
+      // order everywhere. The union holds the top-K unless a CTA whose list
+      // was cut had all MP keys taken; then the two-level path below decides
+      // (shard top-K through L2, then the shards' lists).
+      const int MP = p.mtp, NLS = P * Q;
+      const int nl = local_list(MP);
+      // area layout [BH][P][Q][MP][2]: the group's lists are contiguous
+      const size_t grp = size_t(bh) * NLS * MP * 2;
+      for (int r = 0; r < P; ++r) {
+        unsigned long long* dst = reinterpret_cast<unsigned long long*>(p.peer[r] + p.x_clst) + grp +
+                                  (size_t(pr) * Q + qrank) * MP * 2;
+        for (int i = tid; i < MP; i += kThreads) {
+          const unsigned long long x = i < nl ? lst[i] : 0ull;
+          st_msg(dst + 2 * i, uint32_t(x), epoch);
+          st_msg(dst + 2 * i + 1, uint32_t(x >> 32), epoch);
+        }
+      }
+      const unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_clst) + grp;
+      gather_msgs<true>([src](int i) { return src + i; }, NLS * MP * 2, epoch, p.peer_wait_ns, p.err, reinterpret_cast<float*>(g), tid, kThreads, [](int) { return true; });
+      __syncthreads();
+      const int N = NLS * MP;
+      const int U = hist_keys(g, N, hbk, scratch);
+      const unsigned long long tau = U > K ? kth_key(g, N, K, hbk, bk, scratch, hist, rs) : 0ull;
+      int need = 0;
+      for (int li = warp; li < NLS; li += kThreads / 32) {
+        const int r = li / Q, q = li - (li / Q) * Q;
+        const int nlr = ncand > r ? (ncand - r + P - 1) / P : 0;
+        const int nq = (q + 1) * nlr / Q - q * nlr / Q;
+        int taken = 0;
+        for (int i = lane; i < MP; i += 32) {
+          const unsigned long long x = g[size_t(li) * MP + i];
+          taken += __popc(__ballot_sync(0xffffffffu, x != 0ull && x >= tau));
+        }
+        if (lane == 0) need |= (nq > MP && taken == MP);
+      }
+      if (__syncthreads_or(need) == 0) {
+        kk = min(K, U);
+        const unsigned long long* gc = g;
+        uint2* pk = pick;
+        cta_compact(N, [gc, tau](int i) { return gc[i] != 0ull && gc[i] >= tau; },
+                    [gc, pk, to_pick](int pos, int i) { pk[pos] = to_pick(gc[i]); }, scratch);
+        global_done = true;
+      }
+    }
+    if (global_done) {
+    } else if (K == 0) {
       kk = 0;
     } else if (Q == 1) {
       kk = local_list(K);
@@ -1082,7 +1162,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
         },
         scratch);
     select_union(U);
-  } else if (peer && K > 0) {
+  } else if (peer && K > 0 && !global_done) {
     // Peer mode: (1) this shard's local top-K (0-padded full keys, two
     // message words each) goes into every shard's exchange area; (2) every
     // shard's candidates of the group are read from this shard's area as
@@ -1231,21 +1311,21 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       // the stage's K and V rows, all column boxes: one copy when the K map
       // covers V too (4-D, V one fixed stride after K), else one each
       if (p.kv_fused) {
-        tma_load_4d(st, &tmK, 0, row, 0, 0, full + s);
+        tma_load_4d(st, &tmK, 0, row, 0, 0, full + s, spol);
       } else {
-        tma_load_3d(st, &tmK, 0, row, 0, full + s);
-        tma_load_3d(st + kvb, &tmV, 0, row, 0, full + s);
+        tma_load_3d(st, &tmK, 0, row, 0, full + s, spol);
+        tma_load_3d(st + kvb, &tmV, 0, row, 0, full + s, spol);
       }
       if constexpr (BITS != 0) {
         const size_t so = size_t(row) * NG * sizeof(E);
         uint8_t* sb = st + 2 * kvb;
         if (p.sb_fused) {
-          tma_load_2d(sb, &tmS, int32_t(so), 0, full + s);  // so < 2^31 whenever the map is used
+          tma_load_2d(sb, &tmS, int32_t(so), 0, full + s, spol);  // so < 2^31 whenever the map is used
         } else {
-          bulk_load(sb, static_cast<const uint8_t*>(p.k_scales) + so, sbb, full + s);
-          bulk_load(sb + sbb, static_cast<const uint8_t*>(p.k_biases) + so, sbb, full + s);
-          bulk_load(sb + 2 * sbb, static_cast<const uint8_t*>(p.v_scales) + so, sbb, full + s);
-          bulk_load(sb + 3 * sbb, static_cast<const uint8_t*>(p.v_biases) + so, sbb, full + s);
+          bulk_load(sb, static_cast<const uint8_t*>(p.k_scales) + so, sbb, full + s, spol);
+          bulk_load(sb + sbb, static_cast<const uint8_t*>(p.k_biases) + so, sbb, full + s, spol);
+          bulk_load(sb + 2 * sbb, static_cast<const uint8_t*>(p.v_scales) + so, sbb, full + s, spol);
+          bulk_load(sb + 3 * sbb, static_cast<const uint8_t*>(p.v_biases) + so, sbb, full + s, spol);
         }
       }
       *issued = i + 1;
@@ -1253,7 +1333,11 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     if (lane == 0) {
       fence_proxy_async_shared();
       fence_proxy_async_global();
-      for (int i = 0; i < min(nmine, F::kStages); ++i) issue(i);
+      SD_STAMP_HERE(p, 21);
+      for (int i = 0; i < min(nmine, F::kStages); ++i) {
+        issue(i);
+        if (i == 0) SD_STAMP_HERE(p, 22);
+      }
       SD_STAMP_HERE(p, 8);
     }
     __syncwarp();

@@ -97,11 +97,11 @@ __device__ __forceinline__ float4 lds_f4(uint32_t a) {
   asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
   return v;
 }
-// Streaming 16-byte global load that does not allocate in L1.
-__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+// Streaming 16-byte global load that does not allocate in L1 (L2 policy `pol`).
+__device__ __forceinline__ uint4 ldg_stream(const void* p, uint64_t pol) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p), "l"(pol));
   return v;
 }
 
@@ -251,6 +251,7 @@ template <bool kSys, class Addr, class Want>
 __device__ __noinline__ void gather_msgs(Addr addr, int n, uint32_t epoch, uint64_t limit_ns, int* err, float* dst,
                                             int tid, int nthreads, Want want) {
   constexpr int BATCH = 8;
+#pragma unroll 1
   for (int base = tid; base < n; base += nthreads * BATCH) {
     bool need[BATCH];
 #pragma unroll
@@ -292,10 +293,37 @@ __device__ __noinline__ void gather_msgs(Addr addr, int n, uint32_t epoch, uint6
   }
 }
 
+// L2 policy of the data a launch streams once (block summaries, K/V tiles):
+// evict_first, so that the streamed bytes -- tens of MB per layer -- are
+// replaced before the lines every launch reuses (the kernel's code, message
+// words, per-group state). `plain` gives the default policy instead.
+__device__ __forceinline__ uint64_t stream_policy(bool plain) {
+  uint64_t pol;
+  if (plain)
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+  else
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// 16-byte asynchronous global -> shared copy (L2 only, L2 policy `pol`); the
+// issuing thread waits for its own copies with cp_async_wait<N> (groups of
+// cp_async_commit).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Bulk L2 prefetch of [p, p + bytes) (16-byte aligned, bytes % 16 == 0) by the
 // TMA unit: one instruction for a long contiguous range.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes, uint64_t pol) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p), "r"(bytes), "l"(pol)
+               : "memory");
 }
 
 // Generic-proxy writes -> async-proxy (TMA) reads ordering.
@@ -319,37 +347,38 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// Tiled TMA loads of one box into this CTA's shared memory (no multicast).
+// Tiled TMA loads of one box into this CTA's shared memory (no multicast),
+// with L2 policy `pol`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
-                                            uint64_t* bar) {
+                                            uint64_t* bar, uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
-                                            int32_t w, uint64_t* bar) {
+                                            int32_t w, uint64_t* bar, uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
-                                            uint64_t* bar) {
+                                            uint64_t* bar, uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 // 1-D bulk copy global -> this CTA's shared memory (16-byte aligned, size % 16 == 0).
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
           smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 
@@ -659,9 +688,11 @@ __device__ __noinline__ void radix_select(KeyF keyf, int n, int k, uint32_t* his
   unsigned long long prefix = 0ull, mask = 0ull;
   int rem = k;
   for (int pb = 7; pb >= 0; --pb) {
+#pragma unroll 1
     for (int i = tid; i < 256; i += nthr) hist[i] = 0u;
     __syncthreads();
     const int shift = 8 * pb;
+#pragma unroll 1
     for (int base = warp * 32; base < n; base += nthr) {
       const int i = base + lane;
       bool active = false;
@@ -737,8 +768,10 @@ __device__ __noinline__ unsigned long long topk_threshold(KeyF keyf, int n, int 
   const int tid = threadIdx.x, nthr = blockDim.x;
   unsigned long long* tau = reinterpret_cast<unsigned long long*>(scratch + 122);
   if (!have_hist) {
+#pragma unroll 1
     for (int i = tid; i < kBuckets; i += nthr) h[i] = 0u;
     __syncthreads();
+#pragma unroll 1
     for (int i = tid; i < n; i += nthr) atomicAdd(&h[key_bucket(keyf(i))], 1u);
   }
   __syncthreads();
@@ -747,12 +780,14 @@ __device__ __noinline__ unsigned long long topk_threshold(KeyF keyf, int n, int 
   const int per = (kBuckets + nthr - 1) / nthr;
   const int top = kBuckets - 1 - tid * per;
   int cnt = 0;
+#pragma unroll 1
   for (int j = 0; j < per; ++j)
     if (top - j >= 0) cnt += int(h[top - j]);
   int total;
   const int before = cta_exclusive_scan(cnt, scratch, &total);
   if (before < k && before + cnt >= k) {
     int acc = before;
+#pragma unroll 1
     for (int j = 0; j < per && top - j >= 0; ++j) {
       const int c = int(h[top - j]);
       if (acc + c >= k) {
@@ -773,6 +808,7 @@ __device__ __noinline__ unsigned long long topk_threshold(KeyF keyf, int n, int 
     unsigned long long* bk = reinterpret_cast<unsigned long long*>(bidx);
     cta_compact(n, [&](int i) { return key_bucket(keyf(i)) == b; }, [&](int pos, int i) { bk[pos] = keyf(i); },
                 scratch);
+#pragma unroll 1
     for (int a = tid; a < nb; a += nthr) {
       const unsigned long long x = bk[a];
       int rank = 0;
@@ -784,6 +820,7 @@ __device__ __noinline__ unsigned long long topk_threshold(KeyF keyf, int n, int 
     radix_select(keyf, n, k, hist256, rs);
     const unsigned long long pre = rs->prefix, msk = rs->mask;
     unsigned long long m = ~0ull;
+#pragma unroll 1
     for (int i = tid; i < n; i += nthr) {
       const unsigned long long x = keyf(i);
       if ((x & msk) >= pre && x < m) m = x;
@@ -802,10 +839,9 @@ __device__ __noinline__ unsigned long long topk_threshold(KeyF keyf, int n, int 
 // function; scratch: cta_exclusive_scan's 33 ints, [118, 124).
 // ---------------------------------------------------------------------------
 
-// Shared-memory atomics aimed at one address serialise across a warp, so the
-// selection aggregates them per warp. warp_slot: a slot in a buffer with
-// counter *ctr for every lane whose `want` holds (one atomic per warp); all
-// lanes of the warp call it.
+// A slot in a buffer with counter *ctr for every lane whose `want` holds, one
+// shared atomic per warp (atomics aimed at one address serialise across a
+// warp); all lanes of the warp call it.
 __device__ __forceinline__ int warp_slot(bool want, int* ctr) {
   const unsigned m = __ballot_sync(0xffffffffu, want);
   const int lane = threadIdx.x & 31;
@@ -814,26 +850,18 @@ __device__ __forceinline__ int warp_slot(bool want, int* ctr) {
   base = __shfl_sync(0xffffffffu, base, __ffs(m ? m : 1u) - 1);
   return base + __popc(m & ((1u << lane) - 1u));
 }
-// h[bucket] += 1 for every lane whose `want` holds, one atomic per distinct
-// bucket of the warp; all lanes of the warp call it.
-__device__ __forceinline__ void warp_hist_add(bool want, uint32_t bucket, uint32_t* h) {
-  const unsigned m = __ballot_sync(0xffffffffu, want);
-  if (want) {
-    const unsigned peers = __match_any_sync(m, bucket);
-    if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&h[bucket], uint32_t(__popc(peers)));
-  }
-}
-
 // Bucket histogram of the non-zero keys x[0, n); returns their number.
 static __device__ __noinline__ int hist_keys(const unsigned long long* x, int n, uint32_t* h, int* scratch) {
+#pragma unroll 1
   for (int i = threadIdx.x; i < kBuckets; i += blockDim.x) h[i] = 0u;
   if (threadIdx.x == 0) scratch[118] = 0;
   __syncthreads();
   int c = 0;
+#pragma unroll 1
   for (int b0 = threadIdx.x & ~31; b0 < n; b0 += blockDim.x) {  // whole warps in step
     const int i = b0 + (threadIdx.x & 31);
     const unsigned long long v = i < n ? x[i] : 0ull;
-    warp_hist_add(v != 0ull, key_bucket(v), h);
+    if (v != 0ull) atomicAdd(&h[key_bucket(v)], 1u);
     c += v != 0ull ? 1 : 0;
   }
   c = __reduce_add_sync(0xffffffffu, c);
@@ -857,12 +885,14 @@ static __device__ __noinline__ unsigned long long kth_key(const unsigned long lo
   const int per = (kBuckets + nthr - 1) / nthr;
   const int top = kBuckets - 1 - tid * per;
   int cnt = 0;
+#pragma unroll 1
   for (int j = 0; j < per; ++j)
     if (top - j >= 0) cnt += int(h[top - j]);
   int total;
   const int before = cta_exclusive_scan(cnt, scratch, &total);
   if (before < k && before + cnt >= k) {
     int acc = before;
+#pragma unroll 1
     for (int j = 0; j < per && top - j >= 0; ++j) {
       const int c = int(h[top - j]);
       if (acc + c >= k) {
@@ -882,6 +912,7 @@ static __device__ __noinline__ unsigned long long kth_key(const unsigned long lo
   const int r = k - scratch[121];  // keys still needed from bucket b (>= 1)
   const int nb = int(h[b]);
   if (nb <= 256) {
+#pragma unroll 1
     for (int b0 = tid & ~31; b0 < n; b0 += nthr) {
       const int i = b0 + (tid & 31);
       const unsigned long long v = i < n ? x[i] : 0ull;
@@ -890,6 +921,7 @@ static __device__ __noinline__ unsigned long long kth_key(const unsigned long lo
       if (in) bk[slot] = v;
     }
     __syncthreads();
+#pragma unroll 1
     for (int a = tid; a < nb; a += nthr) {
       const unsigned long long v = bk[a];
       int rank = 0;
@@ -901,6 +933,7 @@ static __device__ __noinline__ unsigned long long kth_key(const unsigned long lo
     radix_select([x](int i) { return x[i]; }, n, k, hist256, rs);
     const unsigned long long pre = rs->prefix, msk = rs->mask;
     unsigned long long m = ~0ull;
+#pragma unroll 1
     for (int i = tid; i < n; i += nthr) {
       const unsigned long long v = x[i];
       if (v && (v & msk) >= pre && v < m) m = v;
@@ -921,6 +954,7 @@ static __device__ __noinline__ int top_keys(const unsigned long long* x, int n, 
                                      uint32_t* hist256, RadixState* rs) {
   const int tid = threadIdx.x, nthr = blockDim.x;
   if (n <= m) {
+#pragma unroll 1
     for (int i = tid; i < n; i += nthr) out[i] = x[i];
     __syncthreads();
     return n;
@@ -930,6 +964,7 @@ static __device__ __noinline__ int top_keys(const unsigned long long* x, int n, 
   const unsigned long long t = kth_key(x, n, m, h, bk, scratch, hist256, rs);
   if (tid == 0) scratch[119] = 0;
   __syncthreads();
+#pragma unroll 1
   for (int b0 = tid & ~31; b0 < n; b0 += nthr) {
     const int i = b0 + (tid & 31);
     const unsigned long long v = i < n ? x[i] : 0ull;

@@ -59,6 +59,10 @@ struct DecodeParams {
   // epoch and the count of finished CTAs.
   uint8_t* peer[8];
   int64_t x_cand, x_part, x_ctl;  // byte offsets inside an area
+  // Sliced selection in peer mode: every CTA's best mtp keys
+  // [P][BH][Q][mtp][2] at x_clst (mtp = 0: the two-level path only).
+  int mtp;
+  int64_t x_clst;
   uint64_t peer_wait_ns;                   // bound of every wait for another shard
   // 1: the scale/bias tensor map covers the four arrays (k_scales, k_biases,
   // v_scales, v_biases at one fixed stride), one copy per tile. 0: four 1-D
@@ -69,6 +73,7 @@ struct DecodeParams {
   int lt;
   int kv_fused;
   unsigned long long* dbg;  // phase-timing build only: [grid.y][grid.x][24] stamps, or null
+  int l2_plain;  // 1: streamed loads (summaries, K/V tiles) without the L2 evict_first hint
 };
 
 struct AppendParams {

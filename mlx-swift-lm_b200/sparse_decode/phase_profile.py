@@ -34,7 +34,8 @@ SUBPHASES = [("select.local_or_cluster_wait", 3, 15), ("select.exchange_or_topk"
              ("merge.gather", 12, 13), ("merge.output", 13, 6),
              ("sliced.keys64", 3, 16), ("sliced.local_list", 16, 15), ("sliced.union_hist", 14, 17),
              ("sliced.union_kth", 17, 18), ("sliced.list_check", 18, 19), ("sliced.picks", 19, 20),
-             ("sliced.after_picks", 20, 4)]
+             ("sliced.after_picks", 20, 4), ("attend.proxy_fences", 4, 21), ("attend.first_issue", 21, 22),
+             ("attend.warp0_unit0", 9, 23), ("attend.warp0_unit8_on", 23, 10)]
 
 
 def _load_phase_lib():
@@ -51,10 +52,12 @@ def _load_phase_lib():
     L.sd_debug_set_phase_buffer.restype = ctypes.c_int32
     L.sd_debug_grid.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]
     L.sd_debug_grid.restype = ctypes.c_int32
+    L.sd_debug_set_l2_plain.argtypes = [ctypes.c_void_p, ctypes.c_int32]
+    L.sd_debug_set_l2_plain.restype = ctypes.c_int32
     return L
 
 
-def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True) -> dict:
+def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True, l2_plain: bool = False) -> dict:
     import torch
 
     L = _load_phase_lib()
@@ -70,6 +73,7 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True) -> 
         k, v = case["k"], case["v"]
         idx.append(k[:, :, : w.T - 1].contiguous(), v[:, :, : w.T - 1].contiguous())
         idx.set_launch_overlap(overlap)
+        _check(L.sd_debug_set_l2_plain(idx._h, 1 if l2_plain else 0))
         gx, gy = ctypes.c_int32(), ctypes.c_int32()
         _check(L.sd_debug_grid(idx._h, ctypes.byref(gx), ctypes.byref(gy)))
         buf = torch.zeros((gy.value, gx.value, 24), dtype=torch.int64, device="cuda")
@@ -133,7 +137,7 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True) -> 
     cad = [(entries[i + 1] - entries[i]) / 1000.0 for i in range(len(entries) - 1)]
     gaps = [(entries[i + 1] - exits[i]) / 1000.0 for i in range(len(entries) - 1)]
     res = {
-        "config": w.name, "layers": layers, "grid": list(items[0]["buf"].shape[:2][::-1]),
+        "config": w.name, "layers": layers, "l2_evict_first_hint": not l2_plain, "grid": list(items[0]["buf"].shape[:2][::-1]),
         "us_per_layer_events": round(us_layer, 3), "device_error": err,
         "algorithmic_bytes_per_layer": algorithmic_bytes(w),
         "phase_us_median_over_ctas": {p: round(statistics.median(per_phase[p]), 3) for p in PHASES},
@@ -154,10 +158,11 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--no-overlap", action="store_true")
+    ap.add_argument("--l2-plain", action="store_true", help="streamed loads without the L2 evict_first hint")
     args = ap.parse_args()
     import torch
     torch.cuda.set_device(0)
-    print(json.dumps(profile(args.config, args.layers, args.warmup, not args.no_overlap)), flush=True)
+    print(json.dumps(profile(args.config, args.layers, args.warmup, not args.no_overlap, args.l2_plain)), flush=True)
 
 
 if __name__ == "__main__":

@@ -70,7 +70,7 @@ def test_cpu_time_reports_threads_and_matches_the_oracle(oracle_lib):
     import numpy as np
 
     import oracle
-    w = CONFIGS["c2q8"].with_(B=1, T=4096)
+    w = CONFIGS["c2q8"].with_(name="c2q8_reduced_B1_T4096", B=1, T=4096)
     inp = bench.cpu_inputs_generated(w, 5)
     us, n, used, out, sel = bench.cpu_time(w, inp, 0.05, 2)
     assert n >= 1 and us > 0.0 and 1 <= used <= 2

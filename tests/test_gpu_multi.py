@@ -19,14 +19,35 @@ pytestmark = pytest.mark.gpu
 CASES = [
     Workload("mg_bf16", B=2, Hq=8, Hkv=2, D=128, T=64 * 40 + 9, S=64, K=8, dtype="bf16", needles=4),
     Workload("mg_q8", B=1, Hq=32, Hkv=8, D=128, T=128 * 20 + 1, S=128, K=5, dtype="bf16", bits=8, needles=3),
+    # K = 256 over 4200 candidates: the sliced selection, whose CTAs' lists
+    # meet across the shards in one exchange
+    Workload("mg_k256_q8", B=1, Hq=8, Hkv=2, D=128, T=64 * 4200 + 7, S=64, K=256, dtype="bf16", bits=8,
+             needles=20),
+    # every candidate block scores the same: the K lowest block indices win,
+    # so the lists of the first CTAs of every shard are cut and fully taken
+    # (the exact two-level path decides)
+    Workload("mg_ties", B=1, Hq=4, Hkv=1, D=128, T=64 * 3001, S=64, K=256, dtype="bf16"),
 ]
+
+
+def _case(i: int):
+    from _util import host_case
+    w = CASES[i]
+    c = host_case(w, 300 + i)
+    if w.name == "mg_ties":
+        from test_gpu_parity import _recompute
+        ks = c["ks"].reshape(1, w.T, w.D)
+        for j in range(1, w.NB - 1):
+            ks[0, j * w.S:(j + 1) * w.S] = ks[0, 0:w.S]
+        c = _recompute(w, c, ks)
+        assert list(c["sel"][0]) == list(range(w.K)) + [w.NB - 1]
+    return c
 
 
 def _rank_main(rank: int, world: int, port: int, results):
     import torch
     import torch.distributed as dist
     from gpu_cases import to_dev, to_host
-    from _util import host_case, rel_err
     from sparse_decode import ShardComm, SparseIndex, sharded_decode
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
@@ -34,7 +55,7 @@ def _rank_main(rank: int, world: int, port: int, results):
     try:
         res = []
         for i, w in enumerate(CASES):
-            c = host_case(w, 300 + i)
+            c = _case(i)
             B, Hkv, T, D = w.B, w.Hkv, w.T, w.D
             idx = SparseIndex(B, w.Hq, Hkv, D, w.S, w.K, T, w.dtype, w.bits, shard_rank=rank, shard_count=world)
             k = to_dev(c["ks"].reshape(B, Hkv, T, D), w.dtype)
@@ -80,7 +101,7 @@ def _free_port() -> int:
 def test_sharded_decode_across_gpus(cuda, world):
     import torch
     import torch.multiprocessing as mp
-    from _util import assert_close, host_case
+    from _util import assert_close
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
@@ -102,7 +123,7 @@ def test_sharded_decode_across_gpus(cuda, world):
     for r in range(world):
         assert not isinstance(got[r], str), f"rank {r}: {got[r]}"
     for i, w in enumerate(CASES):
-        c = host_case(w, 300 + i)
+        c = _case(i)
         ref_out = None
         for r in range(world):
             outs, sels, err = got[r][i]

@@ -20,12 +20,12 @@ pytestmark = pytest.mark.gpu
 
 SMALL = [
     CONFIGS["c0"],                                                     # fp32 D64 G4, the reference CPU-sized case
-    CONFIGS["c1"].with_(T=8192),                                       # bf16 D128 G4 S64 K64
+    CONFIGS["c1"].with_(name="c1_reduced_T8192", T=8192),             # bf16 D128 G4 S64 K64
     Workload("f16_d64_g2", B=2, Hq=4, Hkv=2, D=64, T=3000, S=32, K=16, dtype="f16", needles=5),
     Workload("bf16_g8_s128", B=1, Hq=16, Hkv=2, D=128, T=5000, S=128, K=8, dtype="bf16", needles=3),
     Workload("bf16_g1_s256", B=1, Hq=4, Hkv=4, D=128, T=3333, S=256, K=4, dtype="bf16", needles=2),
-    CONFIGS["c2q8"].with_(B=2, T=8192),                                # 8-bit bf16 scales, outliers
-    CONFIGS["c2q4"].with_(B=2, T=8192),                                # 4-bit
+    CONFIGS["c2q8"].with_(name="c2q8_reduced_B2_T8192", B=2, T=8192),  # 8-bit bf16 scales, outliers
+    CONFIGS["c2q4"].with_(name="c2q4_reduced_B2_T8192", B=2, T=8192),  # 4-bit
     Workload("q8_f16_d64", B=1, Hq=4, Hkv=2, D=64, T=2000, S=64, K=10, dtype="f16", bits=8, needles=3),
     Workload("q4_f32_d64", B=1, Hq=8, Hkv=2, D=64, T=1500, S=32, K=12, dtype="f32", bits=4, needles=3),
     Workload("q4_bf16_d64_g8", B=1, Hq=16, Hkv=2, D=64, T=2500, S=64, K=9, dtype="bf16", bits=4, needles=3),
@@ -88,7 +88,7 @@ def test_many_tiles_per_cta(cuda, bits):
 
 @pytest.mark.parametrize("cluster", [1, 2, 4, 8, 16])
 def test_cluster_sizes_agree(cuda, cluster):
-    w = CONFIGS["c1"].with_(T=6000, K=20)
+    w = CONFIGS["c1"].with_(name="c1_reduced_T6000_K20", T=6000, K=20)
     c, idx, res = run_decode(w, seed=5, cluster=cluster)
     assert idx.cluster_size == cluster
     _check(w, c, res)

@@ -167,3 +167,10 @@ def test_c3_shaped_layer(cuda):
     w = CONFIGS["c3"]
     c, idx, res = run_decode(w, seed=2026)
     _check(w, c, res)
+
+
+def test_c1_full_size_layer(cuda):
+    """Config 1 (bf16, T = 32768, S = 64, top-64 + recent) at full size."""
+    w = CONFIGS["c1"]
+    c, idx, res = run_decode(w, seed=2024)
+    _check(w, c, res, idx)

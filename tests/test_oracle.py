@@ -81,7 +81,7 @@ def test_summaries_match_numpy_twin(oracle_lib, dtype):
 
 
 def test_scores_and_selection_vs_fp64(oracle_lib):
-    w = CONFIGS["c1"].with_(T=8192)
+    w = CONFIGS["c1"].with_(name="c1_reduced_T8192", T=8192)
     c = host_case(w, seed=11)
     sf = oracle.to_f32(c["summ"], c["dt"]).reshape(w.B * w.Hkv, w.NB, w.D)
     s64 = oracle.np_scores_f64(c["q"], sf, w.Hkv, c["scale"])
@@ -110,14 +110,14 @@ def test_select_matches_numpy_and_breaks_ties_low_index(oracle_lib):
 
 
 def test_attend_f64_matches_numpy(oracle_lib):
-    w = CONFIGS["c0"].with_(T=1000, K=4)
+    w = CONFIGS["c0"].with_(name="c0_T1000_K4", T=1000, K=4)
     c = host_case(w, seed=2)
     ref = oracle.np_attend_f64(c["q"], c["Kc"].floats(), c["Vc"].floats(), w.Hkv, w.T, w.S, c["sel"], c["scale"])
     assert np.allclose(c["out"], ref, rtol=1e-12, atol=1e-12)
 
 
 def test_all_blocks_equals_dense_attention(oracle_lib):
-    w = CONFIGS["c0"].with_(T=777, K=64)  # K >= NB - 1: every block
+    w = CONFIGS["c0"].with_(name="c0_T777_K64", T=777, K=64)  # K >= NB - 1: every block
     c = host_case(w, seed=4)
     assert c["sel"].shape[1] == w.NB
     B, Hq, D = w.B, w.Hq, w.D
@@ -144,7 +144,7 @@ def test_needles_are_retrieved(oracle_lib, name):
 
 @pytest.mark.parametrize("bits", [0, 8, 4])
 def test_cpu_baseline_matches_f64(oracle_lib, bits):
-    w = CONFIGS["c2q8"].with_(B=1, T=4096, bits=bits)
+    w = CONFIGS["c2q8"].with_(name=f"c2_reduced_B1_T4096_q{bits}", B=1, T=4096, bits=bits)
     c = host_case(w, seed=8)
     out, sel = oracle.decode_f32(c["qs"], c["dt"], c["Kc"], c["Vc"], c["summ"], c["dt"], w.B, w.Hq, w.Hkv, w.T,
                                  w.S, w.K, c["scale"], threads=2)

@@ -31,7 +31,7 @@ def test_noalloc_decode_matches_sd_decode_twice(cuda, bits):
     from gpu_cases import to_dev, to_host
 
     # 8 (batch, kv-head) groups: several replicas, so the scratch holds partials
-    w = CONFIGS["c1"].with_(T=8192, bits=bits)
+    w = CONFIGS["c1"].with_(name=f"c1_reduced_T8192_q{bits}", T=8192, bits=bits)
     c = host_case(w, seed=77)
     B, Hkv, T, D = w.B, w.Hkv, w.T, w.D
     idx = sd.SparseIndex(B, w.Hq, Hkv, D, w.S, w.K, T, w.dtype, w.bits)
