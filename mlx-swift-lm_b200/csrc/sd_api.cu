@@ -1185,11 +1185,23 @@ extern "C" int32_t sd_decode_noalloc(const sd_config* cfg, const sd_arrays* arra
   auto fits = [&]() { return total(x.C, x.R) <= kNoAllocScratch; };
   // fewer replicas first, then smaller clusters (one CTA per group needs no message words)
   while (!fits() && x.R > 1) --x.R;
+  const int c_chosen = x.C;
   while (!fits() && x.C > 1) {
     int c2 = x.C - 1;
     while (c2 > 1 && ((x.nb_local + c2 - 1) / c2 > sd::kLocalKeysMax || max_active_clusters(&x, c2) < 1)) --c2;
     if ((x.nb_local + c2 - 1) / c2 > sd::kLocalKeysMax) break;
     x.C = c2;
+  }
+  if (x.C < c_chosen && fits()) {
+    // a smaller cluster leaves room for replicas again: raise R while the
+    // scratch holds them and every cluster stays resident at once (the rule
+    // choose_cluster applies)
+    int n_sm = 148;
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, x.device);
+    const int64_t mac = max_active_clusters(&x, x.C);
+    while (x.R < 4 && BH * x.C * (x.R + 1) <= n_sm && mac >= BH * (x.R + 1) &&
+           total(x.C, x.R + 1) <= kNoAllocScratch)
+      ++x.R;
   }
   if (!fits())
     return fail(SD_ERR_CAPACITY, "batch*kv_heads (%lld) needs %zu bytes of scratch; the limit is %zu",

@@ -61,11 +61,11 @@ __device__ __noinline__ int cta_compact(int n, Pred pred, Emit emit, int* scratc
   const int per = (n + blockDim.x - 1) / blockDim.x;
   const int i0 = min(n, int(threadIdx.x) * per), i1 = min(n, i0 + per);
   int cnt = 0;
-#pragma unroll 1
+#pragma unroll 4
   for (int i = i0; i < i1; ++i) cnt += pred(i) ? 1 : 0;
   int total;
   int pos = cta_exclusive_scan(cnt, scratch, &total);
-#pragma unroll 1
+#pragma unroll 4
   for (int i = i0; i < i1; ++i)
     if (pred(i)) emit(pos++, i);
   __syncthreads();
@@ -657,6 +657,230 @@ __device__ __forceinline__ void consume_tiles_qmma(const DecodeParams& p, const 
   }
 }
 
+// 8-bit codes on tensor cores with the tokens as the rows of the m16n8k16
+// tile: S^T = K q^T and O^T = V^T P^T, so the G <= 8 query heads fill the
+// tile's 8 columns (rather than G of its 16 rows): half the mma instructions
+// and accumulators of consume_tiles_qmma. The codes enter as exact fp16
+// values (code_pair_u8); q.k = s_k * (q.c) + b_k * sum(q) per 64-dim group,
+// and p.v = (p * s_v) . c + sum(p * b_v), with p * s_v split into hi + lo
+// fp16 halves. TS token rows per pass (a whole 64-row stage, or 32).
+// Fragments: lane (g, tq) = (lane / 4, lane % 4).
+//   S^T tile (16 tokens x 8 heads): rows g, g + 8 = tokens, columns 2tq, 2tq + 1 = heads.
+//   A of S^T: K codes by ldmatrix; k-slots {2tq, 2tq+1, 2tq+8, 2tq+9} = dims 4tq..4tq+3 of
+//     the 16-dim chunk (q^T, the B operand, is packed in the same order).
+//   B of O^T: P^T by movmatrix from the S^T accumulators (k-slot = token).
+//   A of O^T: V codes by ldmatrix.trans; row g = dim 2g, row g + 8 = dim 2g + 1 of the chunk.
+template <typename E, int D, int G, int TS>
+__device__ __forceinline__ void consume_tiles_q8t(const DecodeParams& p, const TileWalk& tw, const E* qg,
+                                                  const float* qs, int warp, int lane) {
+  using F = Fmt<2, 8, D>;
+  constexpr int MT = TS / 16, NG = F::kGroups, NCH = F::kNChunk;  // NCH = D / 16
+  constexpr int CPG = 4;  // 16-dim chunks per 64-dim quantization group
+  static_assert(G <= 8 && NCH % 2 == 0 && F::kEpc == 16, "8-bit codes, at most 8 heads");
+  static_assert(F::kNBox == 1, "8-bit rows of at most 128 bytes: one box column");
+  const int g = lane >> 2, tq = lane & 3;
+  const int S = p.S, T = p.T;
+  float qmax = 0.0f;
+  for (int i = lane; i < G * D; i += 32) qmax = fmaxf(qmax, fabsf(Elt<E>::to_f32(qg[i])));
+  qmax = warp_max(qmax);
+  const int eq = qmax > 16384.0f ? (ilogbf(qmax) - 13) : 0;
+  const float qscale = ldexpf(1.0f, -eq);
+  auto qv = [&](int d) { return g < G ? Elt<E>::to_f32(qg[g * D + d]) * qscale : 0.0f; };
+  uint32_t qb0[NCH], qb1[NCH];  // q^T of head g: dims 16c + 4tq + {0, 1} and {2, 3}
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int d = 16 * c + 4 * tq;
+    qb0[c] = pack2<__half>(qv(d), qv(d + 1));
+    qb1[c] = pack2<__half>(qv(d + 2), qv(d + 3));
+  }
+  const float qfac = ldexpf(p.scale_log2, eq);  // undoes 2^-eq and applies scale * log2(e)
+  // this lane's heads: 2tq + h
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f}, ob[2][NG];
+  float o[NCH][4];  // O^T of chunk c: (dim 16c + 2g, heads 2tq, 2tq + 1), (dim 16c + 2g + 1, ...)
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int r = 0; r < NG; ++r) ob[h][r] = 0.0f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) o[c][0] = o[c][1] = o[c][2] = o[c][3] = 0.0f;
+  const int mq = lane >> 3, r8 = lane & 7;
+  auto chunk_addr = [&](uint32_t base, int row, int c) {
+    return base + swz(uint32_t(row * F::kBoxBytes + c * 16), F::kCpb);
+  };
+  for (int i = warp; i < tw.nmine; i += kConsumerWarps) {
+    const int s = i % F::kStages;
+    if ((i < F::kStages || wait_issued(tw.issued, i, p.err)) &&
+        mbar_wait(tw.full + s, uint32_t(i / F::kStages) & 1u, p.err)) {
+      if (i == warp && warp == 0 && lane == 0) SD_STAMP_HERE(p, 9);
+      if (i == warp + kConsumerWarps && warp == 0 && lane == 0) SD_STAMP_HERE(p, 23);
+      const int u = tw.u0 + i, li = u / tw.tpb, tile = u % tw.tpb, j = tw.own[li];
+      const int LT = p.lt;  // the stage holds LT tokens: LT / TS passes
+      uint8_t* stage = tw.ring + s * F::kStageBytes;
+      for (int hf = 0; hf < LT / TS; ++hf) {
+      const int nv = min(TS, T - (j * S + tile * LT + hf * TS));
+      if (nv <= 0) break;
+      const uint32_t kb = smem_u32(stage) + uint32_t(hf * TS * F::kBoxBytes);
+      const uint32_t vb = smem_u32(stage) + uint32_t(LT * F::kRowBytes + hf * TS * F::kBoxBytes);
+      const E* ksc = reinterpret_cast<const E*>(stage + 2 * LT * F::kRowBytes) + hf * TS * NG;
+      const E* kbi = ksc + LT * NG;
+      const E* vsc = ksc + 2 * LT * NG;
+      const E* vbi = ksc + 3 * LT * NG;
+      // --- S^T = K q^T per group: m-tile mt = tokens 16mt .. 16mt + 15 ---
+      float acc[NG][MT][4];
+#pragma unroll
+      for (int r = 0; r < NG; ++r)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) acc[r][mt][0] = acc[r][mt][1] = acc[r][mt][2] = acc[r][mt][3] = 0.0f;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+        for (int c = 0; c < NCH; c += 2) {
+          // matrices: tokens 16mt + {0..7, 8..15} of chunks c and c + 1
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4(chunk_addr(kb, 16 * mt + 8 * (mq & 1) + r8, c + (mq >> 1)), r0, r1, r2, r3);
+          mma16816_f16(acc[c / CPG][mt], code_pair_u8(r0, 0x4140u), code_pair_u8(r1, 0x4140u),
+                       code_pair_u8(r0, 0x4342u), code_pair_u8(r1, 0x4342u), qb0[c], qb1[c]);
+          mma16816_f16(acc[(c + 1) / CPG][mt], code_pair_u8(r2, 0x4140u), code_pair_u8(r3, 0x4140u),
+                       code_pair_u8(r2, 0x4342u), code_pair_u8(r3, 0x4342u), qb0[c + 1], qb1[c + 1]);
+        }
+      }
+      // scores (log2 units): token 16mt + g + 8e, head 2tq + h
+      float sc[MT][2][2];
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = 16 * mt + g + 8 * e;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int hd = 2 * tq + h;
+            float v = 0.0f;
+            if (t < nv && hd < G) {
+#pragma unroll
+              for (int r = 0; r < NG; ++r) {
+                const float s_ = Elt<E>::to_f32(ksc[t * NG + r]), b_ = Elt<E>::to_f32(kbi[t * NG + r]);
+                v = fmaf(s_, acc[r][mt][2 * e + h] * qfac, fmaf(b_, qs[hd * NG + r], v));
+              }
+            }
+            sc[mt][e][h] = t < nv ? v : -INFINITY;
+            mx[h] = fmaxf(mx[h], sc[mt][e][h]);
+          }
+        }
+      }
+      float mn[2], alpha[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 4));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 8));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 16));
+        mn[h] = fmaxf(m_run[h], mx[h]);
+        alpha[h] = exp2f(m_run[h] - mn[h]);
+      }
+      float rs[2] = {0.0f, 0.0f}, bsum[2][NG];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int r = 0; r < NG; ++r) bsum[h][r] = 0.0f;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = 16 * mt + g + 8 * e;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            sc[mt][e][h] = t < nv ? exp2f(sc[mt][e][h] - mn[h]) : 0.0f;
+            rs[h] += sc[mt][e][h];
+            if (t < nv) {
+#pragma unroll
+              for (int r = 0; r < NG; ++r)
+                bsum[h][r] = fmaf(sc[mt][e][h], Elt<E>::to_f32(vbi[t * NG + r]), bsum[h][r]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int o_ = 4; o_ <= 16; o_ <<= 1) {
+          rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], o_);
+#pragma unroll
+          for (int r = 0; r < NG; ++r) bsum[h][r] += __shfl_xor_sync(0xffffffffu, bsum[h][r], o_);
+        }
+        l_run[h] = l_run[h] * alpha[h] + rs[h];
+        m_run[h] = mn[h];
+#pragma unroll
+        for (int r = 0; r < NG; ++r) ob[h][r] = ob[h][r] * alpha[h] + bsum[h][r];
+      }
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        o[c][0] *= alpha[0];
+        o[c][1] *= alpha[1];
+        o[c][2] *= alpha[0];
+        o[c][3] *= alpha[1];
+      }
+      // --- O^T += V^T P'^T: k-step kt = tokens 16kt .. 16kt + 15 ---
+#pragma unroll
+      for (int kt = 0; kt < MT; ++kt) {
+        // P' = p * s_v per group as hi + lo fp16 in the S^T layout (tokens
+        // 16kt + g, + 8; heads 2tq, 2tq + 1), transposed into B fragments
+        // (tokens 2tq, 2tq + 1 and 8 + 2tq, 8 + 2tq + 1 of head g); the code
+        // and bias parts of p.v can nearly cancel, so p' keeps ~22 bits
+        uint32_t bh0[NG], bh1[NG], bl0[NG], bl1[NG];
+        const int t0 = 16 * kt + g, t1 = t0 + 8;
+#pragma unroll
+        for (int r = 0; r < NG; ++r) {
+          const float s0 = t0 < nv ? Elt<E>::to_f32(vsc[t0 * NG + r]) : 0.0f;
+          const float s1 = t1 < nv ? Elt<E>::to_f32(vsc[t1 * NG + r]) : 0.0f;
+          uint32_t h0, l0, h1, l1;
+          split2<__half>(sc[kt][0][0] * s0, sc[kt][0][1] * s0, h0, l0);
+          split2<__half>(sc[kt][1][0] * s1, sc[kt][1][1] * s1, h1, l1);
+          bh0[r] = movm_trans(h0);
+          bl0[r] = movm_trans(l0);
+          bh1[r] = movm_trans(h1);
+          bl1[r] = movm_trans(l1);
+        }
+#pragma unroll
+        for (int c = 0; c < NCH; c += 2) {
+          // matrices (transposed): tokens 16kt + {0..7, 8..15} of chunks c and c + 1
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4_t(chunk_addr(vb, 16 * kt + 8 * (mq & 1) + r8, c + (mq >> 1)), r0, r1, r2, r3);
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int cc = c + hh, grp = cc / CPG;
+            const uint32_t ra = hh ? r2 : r0, rb = hh ? r3 : r1;
+            const uint32_t a0 = code_pair_u8(ra, 0x4240u), a1 = code_pair_u8(ra, 0x4341u);
+            const uint32_t a2 = code_pair_u8(rb, 0x4240u), a3 = code_pair_u8(rb, 0x4341u);
+            mma16816_f16(o[cc], a0, a1, a2, a3, bh0[grp], bh1[grp]);
+            mma16816_f16(o[cc], a0, a1, a2, a3, bl0[grp], bl1[grp]);
+          }
+        }
+      }
+      }  // passes over the stage
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tw.empty + s);
+  }
+  if (warp == 0 && lane == 0) SD_STAMP_HERE(p, 10);
+  named_barrier(1, kConsumerWarps * 32);  // all consumers are done with the ring
+  float* w = tw.mw + warp * (G * D + 2 * G);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int hd = 2 * tq + h;
+    if (hd < G) {
+      if (g == 0) { w[hd] = m_run[h]; w[G + hd] = l_run[h]; }
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int d = 16 * c + 2 * g + e;
+          w[2 * G + hd * D + d] = o[c][2 * e + h] + ob[h][d / 64];
+        }
+      }
+    }
+  }
+}
+
 template <typename E, int BITS, int D, int G>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap tmK,
@@ -1134,18 +1358,31 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       SD_STAMP_C(p, 20);
     }
   }
-  // The group's top-K of a candidate union uni[0, U) (score key, block), by
-  // radix select; every shard computes the same selection.
+  // The group's top-K of a candidate union uni[0, U) (score key, block):
+  // the pairs become 64-bit keys in place, then the bucket histogram finds
+  // the K-th key and the keys at or above it are kept in union order; every
+  // shard computes the same selection.
   auto select_union = [&](int U) {
     kk = min(K, U);
-    auto ukey = [&](int i) -> unsigned long long { return full_key(uni[i].x, int32_t(uni[i].y)); };
+    unsigned long long* uk64 = reinterpret_cast<unsigned long long*>(uni);
+    for (int i = tid; i < U; i += kThreads) {
+      const uint2 e = uni[i];
+      uk64[i] = full_key(e.x, int32_t(e.y));
+    }
+    __syncthreads();
+    const unsigned long long* ukc = uk64;
+    uint2* pk = pick;
+    auto emit = [ukc, pk](int pos, int i) {
+      pk[pos] = make_uint2(uint32_t(ukc[i] >> 32), 0xffffffffu - uint32_t(ukc[i]));
+    };
     if (U > K && K > 0) {
-      radix_select(ukey, U, K, hist, rs);
-      const unsigned long long pre = rs->prefix, msk = rs->mask;
-      cta_compact(U, [&](int i) { return (ukey(i) & msk) >= pre; }, [&](int pos, int i) { pick[pos] = uni[i]; },
-                  scratch);
+      hist_keys(uk64, U, hbk, scratch);
+      const unsigned long long tau = kth_key(uk64, U, K, hbk,
+                                             reinterpret_cast<unsigned long long*>(sm + L.ring + 144 * 1024),
+                                             scratch, hist, rs);
+      cta_compact(U, [ukc, tau](int i) { return ukc[i] >= tau; }, emit, scratch);
     } else {
-      for (int i = tid; i < kk; i += kThreads) pick[i] = uni[i];
+      for (int i = tid; i < kk; i += kThreads) emit(i, i);
       __syncthreads();
     }
   };
@@ -1362,6 +1599,11 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     __syncwarp();
   } else if constexpr (kMma) {
     consume_tiles_mma<E, D, G>(p, tw, qg, warp, lane);
+  } else if constexpr (kQMma && BITS == 8) {
+    // a 64-row stage in one pass (4 m-tiles of tokens: twice the independent
+    // mma chains per softmax step), else 32 rows per pass
+    if (LT == 64) consume_tiles_q8t<E, D, G, 64>(p, tw, qg, qs, warp, lane);
+    else consume_tiles_q8t<E, D, G, kTileTokens>(p, tw, qg, qs, warp, lane);
   } else if constexpr (kQMma) {
     consume_tiles_qmma<E, BITS, D, G>(p, tw, qg, qs, warp, lane);
   } else {

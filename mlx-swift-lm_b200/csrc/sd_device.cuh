@@ -411,6 +411,21 @@ __device__ __forceinline__ void mma16816<__half>(float* c, uint32_t a0, uint32_t
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
+// c += A(16x16, row-major) * B(16x8, col-major), all four A registers (fp16).
+__device__ __forceinline__ void mma16816_f16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Transpose of an 8x8 16-bit matrix held one row pair per lane (lane l:
+// row l/4, elements 2(l%4), 2(l%4)+1) into the same layout.
+__device__ __forceinline__ uint32_t movm_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
 // Two floats -> packed 16-bit pair (x in the low half), round to nearest even.
 template <typename E> __device__ __forceinline__ uint32_t pack2(float x, float y);
 template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float x, float y) {
@@ -850,22 +865,52 @@ __device__ __forceinline__ int warp_slot(bool want, int* ctr) {
   base = __shfl_sync(0xffffffffu, base, __ffs(m ? m : 1u) - 1);
   return base + __popc(m & ((1u << lane) - 1u));
 }
-// Bucket histogram of the non-zero keys x[0, n); returns their number.
+// Buckets of the keys' histogram, by the distance d = hi - key of the 32-bit
+// score key from the largest one (hi, kept in scratch[113] by hist_keys): d's
+// binary exponent and 7 mantissa bits, i.e. buckets 1/128 of d wide -- fine
+// near the top, where the K-th key lies, whatever the scores' magnitude and
+// however far outliers sit above the rest. Monotonic: bucket order is key
+// order (bucket kBuckets - 1 holds the largest key).
+__device__ __forceinline__ uint32_t range_bucket(unsigned long long x, uint32_t hi) {
+  const uint32_t d = hi - uint32_t(x >> 32);
+  const uint32_t f = __float_as_uint(__uint2float_rz(d));  // d >= 1: exponent 127..158
+  const uint32_t idx = d == 0u ? 0u : 1u + ((f >> 23) - 127u) * 128u + ((f >> 16) & 127u);
+  return uint32_t(kBuckets - 1) - min(idx, uint32_t(kBuckets - 1));
+}
+// Bucket histogram of the non-zero keys x[0, n) by their distance from the
+// largest; returns their number.
 static __device__ __noinline__ int hist_keys(const unsigned long long* x, int n, uint32_t* h, int* scratch) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll 1
   for (int i = threadIdx.x; i < kBuckets; i += blockDim.x) h[i] = 0u;
-  if (threadIdx.x == 0) scratch[118] = 0;
-  __syncthreads();
-  int c = 0;
-#pragma unroll 1
-  for (int b0 = threadIdx.x & ~31; b0 < n; b0 += blockDim.x) {  // whole warps in step
-    const int i = b0 + (threadIdx.x & 31);
-    const unsigned long long v = i < n ? x[i] : 0ull;
-    if (v != 0ull) atomicAdd(&h[key_bucket(v)], 1u);
-    c += v != 0ull ? 1 : 0;
+  if (threadIdx.x == 0) {
+    scratch[118] = 0;
+    scratch[113] = 0;
   }
+  uint32_t hi = 0u;
+  int c = 0;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long v = x[i];
+    if (v != 0ull) {
+      hi = max(hi, uint32_t(v >> 32));
+      ++c;
+    }
+  }
+  hi = __reduce_max_sync(0xffffffffu, hi);
   c = __reduce_add_sync(0xffffffffu, c);
-  if ((threadIdx.x & 31) == 0 && c) atomicAdd(&scratch[118], c);
+  __syncthreads();  // the counters above are initialised
+  if (lane == 0) {
+    atomicMax(reinterpret_cast<unsigned*>(&scratch[113]), hi);
+    if (c) atomicAdd(&scratch[118], c);
+  }
+  __syncthreads();
+  hi = uint32_t(scratch[113]);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long v = x[i];
+    if (v != 0ull) atomicAdd(&h[range_bucket(v, hi)], 1u);
+  }
   __syncthreads();
   const int total = scratch[118];
   __syncthreads();
@@ -873,10 +918,11 @@ static __device__ __noinline__ int hist_keys(const unsigned long long* x, int n,
 }
 
 // The k-th largest non-zero key of x[0, n) (1 <= k <= number of non-zero
-// keys), h being the bucket histogram of x: the bucket holding it is found
-// from h; that bucket's keys (usually a few dozen) are gathered into bk (256
-// entries) and ranked by counting. A bucket of more than 256 keys (equal
-// scores) is resolved by a radix select over x instead.
+// keys), h being the bucket histogram of x made by hist_keys (whose largest
+// score key is still in scratch): the bucket holding it is found from h; that
+// bucket's keys (usually a few) are gathered into bk (256 entries) and ranked
+// by counting. A bucket of more than 256 keys (equal scores) is resolved by a
+// radix select over x instead.
 static __device__ __noinline__ unsigned long long kth_key(const unsigned long long* x, int n, int k, const uint32_t* h,
                                                    unsigned long long* bk, int* scratch, uint32_t* hist256,
                                                    RadixState* rs) {
@@ -912,11 +958,12 @@ static __device__ __noinline__ unsigned long long kth_key(const unsigned long lo
   const int r = k - scratch[121];  // keys still needed from bucket b (>= 1)
   const int nb = int(h[b]);
   if (nb <= 256) {
-#pragma unroll 1
+    const uint32_t hi = uint32_t(scratch[113]);
+#pragma unroll 4
     for (int b0 = tid & ~31; b0 < n; b0 += nthr) {
       const int i = b0 + (tid & 31);
       const unsigned long long v = i < n ? x[i] : 0ull;
-      const bool in = v != 0ull && key_bucket(v) == b;
+      const bool in = v != 0ull && range_bucket(v, hi) == b;
       const int slot = warp_slot(in, &scratch[119]);
       if (in) bk[slot] = v;
     }
@@ -964,7 +1011,7 @@ static __device__ __noinline__ int top_keys(const unsigned long long* x, int n, 
   const unsigned long long t = kth_key(x, n, m, h, bk, scratch, hist256, rs);
   if (tid == 0) scratch[119] = 0;
   __syncthreads();
-#pragma unroll 1
+#pragma unroll 4
   for (int b0 = tid & ~31; b0 < n; b0 += nthr) {
     const int i = b0 + (tid & 31);
     const unsigned long long v = i < n ? x[i] : 0ull;

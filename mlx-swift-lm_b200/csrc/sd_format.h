@@ -67,7 +67,7 @@ struct Layout {
   int sel;         // (kMaxTopK + 2) ints: selected blocks, ascending, recent last
   int own;         // (kMaxTopK + 2) ints: the selected blocks stored on this shard
   int hist;        // 256 u32
-  int scratch;     // 128 ints: scans [0,33), radix state [40,48), selection tables [64,112)
+  int scratch;     // 128 ints: scans [0,33), radix state [40,48), largest key [113], selection [118,124), ring/own counters [124,127)
   int ps;          // per consumer warp: kTileTokens * G * groups floats
   int cpart;       // G*(D+2) floats: this CTA's merged (m, l, o)
   int recv;        // (m, l) of every CTA of the group for this CTA's output slice

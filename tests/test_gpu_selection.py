@@ -4,11 +4,13 @@ The decode kernel selects the top-K blocks in one of two ways. When a
 group has at most 2048 candidate blocks and K <= 128, every CTA of the group
 holds all candidate keys and runs a block-wide bitonic top-K. Otherwise
 (config 4: 16383 candidates, K = 256) the candidates are split over all the
-group's CTAs, each CTA reduces its share to a sorted list of its best keys,
-and the lists are combined through L2. These cases force the second path --
-K > 128 alone, more than 2048 candidates alone, both, ties across CTAs, and a
-reduced config 4 -- and compare block scores and selected blocks with the
-oracle bit for bit, outputs within the tolerance of tests/_util.py.
+group's CTAs, each CTA reduces its share to a list of its best keys, and the
+lists are combined through L2 (a second round with full lists when a cut
+list was fully taken). These cases force the second path -- K > 128 alone,
+more than 2048 candidates alone, both, 17000 candidates over 64 CTAs, ties
+across CTAs, and a reduced config 4 -- and compare block scores and selected
+blocks with the oracle bit for bit, outputs within the tolerance of
+tests/_util.py.
 Selection semantics: top-K blocks by (score desc, block index asc) plus the
 recent block, ascending.
 """
@@ -36,6 +38,9 @@ LARGE = [
              needles=30),
     # config 4's shape at a quarter of its context: 8-bit, K = 256, 4095 candidates, drift
     CONFIGS["c4"].with_(name="c4_reduced_T262144", T=262144, layers=1),
+    # 17000 candidates in one group, spread over 64 CTAs
+    Workload("sel_k100_n17000", B=1, Hq=4, Hkv=1, D=128, T=64 * 17000 + 3, S=64, K=100, dtype="bf16",
+             bits=8, needles=12),
 ]
 
 
