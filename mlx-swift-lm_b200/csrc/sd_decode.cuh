@@ -1198,9 +1198,10 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     // every CTA takes the same branch.
     const int MT = p.mt;
     // ring map of this path: [0, 16K) local keys as 64-bit keys (or the u32
-    // keys of a large chunk below 64K) -- later the picks; [64K, 128K) the
-    // gathered lists; [128K, 144K) bucket histogram; [144K, 146K) a bucket's
-    // keys; [146K, 154K) this CTA's list.
+    // keys of a large chunk below 64K) -- later the picks; [16K, 32K) sorted
+    // runs of the bitonic local list; [64K, 128K) the gathered lists;
+    // [128K, 144K) bucket histogram; [144K, 146K) a bucket's keys;
+    // [146K, 154K) this CTA's list.
     unsigned long long* lk = reinterpret_cast<unsigned long long*>(sm + L.ring);
     unsigned long long* g = reinterpret_cast<unsigned long long*>(sm + L.ring + 64 * 1024);
     unsigned long long* bk = reinterpret_cast<unsigned long long*>(sm + L.ring + 144 * 1024);
@@ -1208,19 +1209,29 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     const uint32_t* keys_c = keys;
     const int cb = c0, Pc = P, prc = pr;
     auto keyf = [=](int i) -> unsigned long long { return full_key(keys_c[i], (cb + i) * Pc + prc); };
-    const bool small_n = n <= kAllKeysMax;  // the keys live in allk: materialise them as 64-bit keys
-    if (small_n) {
-      for (int i = tid; i < n; i += kThreads) lk[i] = keyf(i);
-      __syncthreads();
-    }
+    const bool small_n = n <= kAllKeysMax;  // the keys live in allk
     SD_STAMP_C(p, 16);
-    bool hist_ready = false;
+    bool lk_ready = false;
     // this CTA's best m keys into lst, in no particular order; returns how many
     auto local_list = [&](int m) -> int {
-      if (small_n) {
-        const int c = top_keys(lk, n, m, hbk, hist_ready, lst, bk, scratch, hist, rs);
-        hist_ready = false;
+      if (small_n && m <= 128) {
+        // bitonic: runs of 64 (m <= 64) or 128 keys sorted in registers by
+        // the warps, merged pairwise; runs[0, m) = the top m, descending
+        unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 16 * 1024);
+        if (m <= 64) block_topk<2>(keyf, n, runs, lane, warp, kThreads / 32);
+        else block_topk<4>(keyf, n, runs, lane, warp, kThreads / 32);
+        const int c = min(n, m);
+        for (int i = tid; i < c; i += kThreads) lst[i] = runs[i];
+        __syncthreads();
         return c;
+      }
+      if (small_n) {
+        if (!lk_ready) {  // the keys as 64-bit keys, once
+          for (int i = tid; i < n; i += kThreads) lk[i] = keyf(i);
+          __syncthreads();
+          lk_ready = true;
+        }
+        return top_keys(lk, n, m, hbk, false, lst, bk, scratch, hist, rs);
       }
       if (n <= m) {
         for (int i = tid; i < n; i += kThreads) lst[i] = keyf(i);

@@ -763,10 +763,10 @@ __device__ __noinline__ void radix_select(KeyF keyf, int n, int k, uint32_t* his
   __syncthreads();
 }
 
-// Buckets of the top-K threshold search: the top 12 bits of a 64-bit key
-// (sign, exponent and 3 mantissa bits of the score).
-constexpr int kBuckets = 4096;
-__device__ __forceinline__ uint32_t key_bucket(unsigned long long x) { return uint32_t(x >> 52); }
+// Buckets of the top-K threshold search over a CTA's own large chunk: the
+// top 10 bits of a 64-bit key (sign, exponent and 1 mantissa bit of the score).
+constexpr int kBuckets = 1024;
+__device__ __forceinline__ uint32_t key_bucket(unsigned long long x) { return uint32_t(x >> 54); }
 
 // The k-th largest of n distinct 64-bit keys keyf(i) (0 < k < n), i.e. the
 // threshold tau with exactly k keys >= tau. A histogram of the keys' buckets
@@ -867,14 +867,15 @@ __device__ __forceinline__ int warp_slot(bool want, int* ctr) {
 }
 // Buckets of the keys' histogram, by the distance d = hi - key of the 32-bit
 // score key from the largest one (hi, kept in scratch[113] by hist_keys): d's
-// binary exponent and 7 mantissa bits, i.e. buckets 1/128 of d wide -- fine
+// binary exponent and 5 mantissa bits, i.e. buckets 1/32 of d wide -- fine
 // near the top, where the K-th key lies, whatever the scores' magnitude and
 // however far outliers sit above the rest. Monotonic: bucket order is key
 // order (bucket kBuckets - 1 holds the largest key).
 __device__ __forceinline__ uint32_t range_bucket(unsigned long long x, uint32_t hi) {
+  static_assert(kBuckets == 32 * 32, "32 binary exponents x 5 mantissa bits");
   const uint32_t d = hi - uint32_t(x >> 32);
   const uint32_t f = __float_as_uint(__uint2float_rz(d));  // d >= 1: exponent 127..158
-  const uint32_t idx = d == 0u ? 0u : 1u + ((f >> 23) - 127u) * 128u + ((f >> 16) & 127u);
+  const uint32_t idx = d == 0u ? 0u : 1u + ((f >> 23) - 127u) * 32u + ((f >> 18) & 31u);
   return uint32_t(kBuckets - 1) - min(idx, uint32_t(kBuckets - 1));
 }
 // Bucket histogram of the non-zero keys x[0, n) by their distance from the
