@@ -1261,6 +1261,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       // (shard top-K through L2, then the shards' lists).
       const int MP = p.mtp, NLS = P * Q;
       const int nl = local_list(MP);
+      SD_STAMP_C(p, 15);
       // area layout [BH][P][Q][MP][2]: the group's lists are contiguous
       const size_t grp = size_t(bh) * NLS * MP * 2;
       for (int r = 0; r < P; ++r) {
@@ -1275,9 +1276,12 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       const unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.peer[pr] + p.x_clst) + grp;
       gather_msgs<true>([src](int i) { return src + i; }, NLS * MP * 2, epoch, p.peer_wait_ns, p.err, reinterpret_cast<float*>(g), tid, kThreads, [](int) { return true; });
       __syncthreads();
+      SD_STAMP_C(p, 14);
       const int N = NLS * MP;
       const int U = hist_keys(g, N, hbk, scratch);
+      SD_STAMP_C(p, 17);
       const unsigned long long tau = U > K ? kth_key(g, N, K, hbk, bk, scratch, hist, rs) : 0ull;
+      SD_STAMP_C(p, 18);
       int need = 0;
       for (int li = warp; li < NLS; li += kThreads / 32) {
         const int r = li / Q, q = li - (li / Q) * Q;
@@ -1290,13 +1294,16 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
         }
         if (lane == 0) need |= (nq > MP && taken == MP);
       }
-      if (__syncthreads_or(need) == 0) {
+      const bool cut = __syncthreads_or(need) != 0;
+      SD_STAMP_C(p, 19);
+      if (!cut) {
         kk = min(K, U);
         const unsigned long long* gc = g;
         uint2* pk = pick;
         cta_compact(N, [gc, tau](int i) { return gc[i] != 0ull && gc[i] >= tau; },
                     [gc, pk, to_pick](int pos, int i) { pk[pos] = to_pick(gc[i]); }, scratch);
         global_done = true;
+        SD_STAMP_C(p, 20);
       }
     }
     if (global_done) {

@@ -13,7 +13,11 @@ does not write is left out), plus the layer cadence seen by %globaltimer.
 
     python -m sparse_decode.phase_profile --config c1 --layers 36
 
-Run from mlx-swift-lm_b200/ (or with it on sys.path); needs a GPU.
+Run from mlx-swift-lm_b200/ (or with it on sys.path); needs a GPU. Under
+torchrun (WORLD_SIZE > 1) every rank profiles its shard of the layers through
+the fused peer-memory step, and rank 0 reports its own CTAs:
+
+    torchrun --nproc-per-node 2 -m sparse_decode.phase_profile --config c4 --layers 8
 """
 from __future__ import annotations
 
@@ -61,15 +65,28 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True, l2_
     import torch
 
     L = _load_phase_lib()
-    from sparse_decode import SparseIndex, _check
+    from sparse_decode import ShardComm, SparseIndex, _check
     from sparse_decode.synth import CONFIGS, algorithmic_bytes, make_case_torch
 
+    # under torchrun: this rank's shard of every layer, the fused peer-memory step
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     w = CONFIGS[config].with_(layers=layers)
     scale = 1.0 / math.sqrt(w.D)
     items = []
     for l in range(layers):
         case = make_case_torch(w, seed=1000 + l)
-        idx = SparseIndex(w.B, w.Hq, w.Hkv, w.D, w.S, w.K, w.T, w.dtype, w.bits)
+        idx = SparseIndex(w.B, w.Hq, w.Hkv, w.D, w.S, w.K, w.T, w.dtype, w.bits, shard_rank=rank,
+                          shard_count=world)
         k, v = case["k"], case["v"]
         idx.append(k[:, :, : w.T - 1].contiguous(), v[:, :, : w.T - 1].contiguous())
         idx.set_launch_overlap(overlap)
@@ -82,20 +99,32 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True, l2_
                       "v": v[:, :, w.T - 1].contiguous(), "out": torch.empty_like(case["q"]), "buf": buf})
         del case, k, v
     torch.cuda.synchronize()
+    comm = ShardComm(items[0]["idx"]) if world > 1 else None
+    if dist:
+        dist.barrier()
+
+    def step(it):
+        if comm is None:
+            it["idx"].decode(it["q"], it["k"], it["v"], scale, out=it["out"])
+        else:
+            it["idx"].shard_decode(comm, it["q"], it["k"], it["v"], scale, out=it["out"])
+
     for it in items:
-        it["idx"].decode(it["q"], it["k"], it["v"], scale, out=it["out"])
+        step(it)
     for it in items:
         it["idx"].trim(1)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         for it in items:
-            it["idx"].decode(it["q"], it["k"], it["v"], scale, out=it["out"])
+            step(it)
     for it in items:
         it["idx"].trim(1)
     for _ in range(warmup):
         graph.replay()
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     graph.replay()
@@ -137,7 +166,7 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True, l2_
     cad = [(entries[i + 1] - entries[i]) / 1000.0 for i in range(len(entries) - 1)]
     gaps = [(entries[i + 1] - exits[i]) / 1000.0 for i in range(len(entries) - 1)]
     res = {
-        "config": w.name, "layers": layers, "l2_evict_first_hint": not l2_plain, "grid": list(items[0]["buf"].shape[:2][::-1]),
+        "config": w.name, "layers": layers, "shards": world, "rank": rank, "l2_evict_first_hint": not l2_plain, "grid": list(items[0]["buf"].shape[:2][::-1]),
         "us_per_layer_events": round(us_layer, 3), "device_error": err,
         "algorithmic_bytes_per_layer": algorithmic_bytes(w),
         "phase_us_median_over_ctas": {p: round(statistics.median(per_phase[p]), 3) for p in PHASES},
@@ -149,6 +178,11 @@ def profile(config: str, layers: int, warmup: int = 3, overlap: bool = True, l2_
         "gap_next_entry_minus_exit_us": round(statistics.median(gaps), 3) if gaps else None,
     }
     del graph
+    if comm is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
+        dist.destroy_process_group()
     return res
 
 
@@ -161,8 +195,11 @@ def main() -> None:
     ap.add_argument("--l2-plain", action="store_true", help="streamed loads without the L2 evict_first hint")
     args = ap.parse_args()
     import torch
-    torch.cuda.set_device(0)
-    print(json.dumps(profile(args.config, args.layers, args.warmup, not args.no_overlap, args.l2_plain)), flush=True)
+    if int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        torch.cuda.set_device(0)
+    res = profile(args.config, args.layers, args.warmup, not args.no_overlap, args.l2_plain)
+    if res["rank"] == 0:
+        print(json.dumps(res), flush=True)
 
 
 if __name__ == "__main__":
