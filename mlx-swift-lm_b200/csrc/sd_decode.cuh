@@ -1210,15 +1210,11 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
     const int cb = c0, Pc = P, prc = pr;
     auto keyf = [=](int i) -> unsigned long long { return full_key(keys_c[i], (cb + i) * Pc + prc); };
     const bool small_n = n <= kAllKeysMax;  // the keys live in allk
-    // every CTA of the group has at most kAllKeysMax candidates (the same
-    // answer on every CTA): lists of at most 128 keys come out sorted
-    const bool chunks_small = (nloc + NCH - 1) / NCH <= kAllKeysMax;
     SD_STAMP_C(p, 16);
     bool lk_ready = false;
-    // this CTA's best m keys into lst (descending when chunks_small and
-    // m <= 128, else in no particular order); returns how many
+    // this CTA's best m keys into lst, in no particular order; returns how many
     auto local_list = [&](int m) -> int {
-      if (chunks_small && m <= 128) {
+      if (small_n && m <= 128) {
         // bitonic: runs of 64 (m <= 64) or 128 keys sorted in registers by
         // the warps, merged pairwise; runs[0, m) = the top m, descending
         unsigned long long* runs = reinterpret_cast<unsigned long long*>(sm + L.ring + 16 * 1024);
@@ -1336,29 +1332,9 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       exchange(p.clist + size_t(bh) * Q * MT * 2, MT, nl1);
       SD_STAMP_C(p, 14);
       int N = Q * MT;
-      // Sorted lists, K <= 256 and Q <= 32: the lists are runs of a bitonic
-      // merge (0-padded to 256 keys each, at the ring's start), merged
-      // pairwise until the first run holds the union's top 256, descending.
-      // Otherwise a histogram threshold over the gathered lists.
-      const bool merge_lists = chunks_small && MT <= 128 && K <= 256 && Q <= 32;
-      constexpr int LU = 256;
-      unsigned long long* ur = reinterpret_cast<unsigned long long*>(sm + L.ring);  // Q * 2 KB <= 64 KB
-      int U;
-      unsigned long long tau;
-      if (merge_lists) {
-        for (int i = tid; i < Q * LU; i += kThreads) {
-          const int q = i / LU, e = i - q * LU;
-          ur[i] = e < MT ? g[size_t(q) * MT + e] : 0ull;
-        }
-        __syncthreads();
-        block_merge_runs<LU / 32>(ur, Q, lane, warp, kThreads / 32, [] { __syncthreads(); });
-        U = __syncthreads_count(tid < K && ur[tid] != 0ull);  // nonzero keys among the top K
-        tau = U == K ? ur[K - 1] : 0ull;
-      } else {
-        U = hist_keys(g, N, hbk, scratch);
-      }
+      int U = hist_keys(g, N, hbk, scratch);
       SD_STAMP_C(p, 17);
-      if (!merge_lists) tau = U > K ? kth_key(g, N, K, hbk, bk, scratch, hist, rs) : 0ull;
+      unsigned long long tau = U > K ? kth_key(g, N, K, hbk, bk, scratch, hist, rs) : 0ull;
       SD_STAMP_C(p, 18);
       bool fallback = false;
       if (MT < K) {
@@ -1390,20 +1366,13 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       // the epoch: CTA 0 holds every list, so every CTA has read the epoch.
       if (p.mode == MODE_CANDIDATES && qrank == 0 && tid == 0) p.gep[bh] = gep;
       kk = min(K, U);
-      if (merge_lists && !fallback) {
-        // the merged run's first kk keys, descending (pick aliases the run:
-        // every thread rewrites only its own entries)
-        for (int i = tid; i < kk; i += kThreads) pick[i] = to_pick(ur[i]);
-        __syncthreads();
-      } else {
-        // the selected keys in the order of the gathered lists: the same
-        // order on every CTA of the group
-        const unsigned long long* gc = g;
-        const unsigned long long tc = tau;
-        uint2* pk = pick;
-        cta_compact(N, [gc, tc](int i) { return gc[i] != 0ull && gc[i] >= tc; },
-                    [gc, pk, to_pick](int pos, int i) { pk[pos] = to_pick(gc[i]); }, scratch);
-      }
+      // the selected keys in the order of the gathered lists: the same order
+      // on every CTA of the group
+      const unsigned long long* gc = g;
+      const unsigned long long tc = tau;
+      uint2* pk = pick;
+      cta_compact(N, [gc, tc](int i) { return gc[i] != 0ull && gc[i] >= tc; },
+                  [gc, pk, to_pick](int pos, int i) { pk[pos] = to_pick(gc[i]); }, scratch);
       SD_STAMP_C(p, 20);
     }
   }
