@@ -539,7 +539,8 @@ def main() -> None:
 
 
 def _check_shards(w, dist, rank: int, world: int, L0, sel0, out0, scale) -> dict:
-    """Every rank's selection and output of layer 0 must be identical; rank 0
+    """Every rank's selection and output of layer 0 must be identical, and
+    equal to what the timed graph replays left in layer 0's output; rank 0
     also decodes layer 0 on one GPU (a single-shard index of the same data)
     and compares: selection equal, output within 2e-3 (normwise)."""
     import numpy as np
@@ -552,6 +553,11 @@ def _check_shards(w, dist, rank: int, world: int, L0, sel0, out0, scale) -> dict
     dist.all_gather(outs, out0)
     same_sel = all(torch.equal(s, sels[0]) for s in sels)
     same_out = all(torch.equal(o, outs[0]) for o in outs)
+    # the timed CUDA-graph replays (launches overlapping across layers) left
+    # layer 0's output of the same token: the same bits as the eager decode
+    graph_ok = torch.tensor([1 if torch.equal(L0["out"], out0) else 0], device="cuda")
+    dist.all_reduce(graph_ok, op=dist.ReduceOp.MIN)
+    graph_same = bool(graph_ok.item())
     ref_sel_ok, ref_err = True, 0.0
     if rank == 0:
         case = make_case_torch(w, seed=L0["seed"])
@@ -565,9 +571,11 @@ def _check_shards(w, dist, rank: int, world: int, L0, sel0, out0, scale) -> dict
         ref_err = _rel_err(_to_f32(out0), _to_f32(o1))
         del one, case
         torch.cuda.empty_cache()
-    flag = torch.tensor([1 if (same_sel and same_out and ref_sel_ok and ref_err <= 2e-3) else 0], device="cuda")
+    flag = torch.tensor([1 if (same_sel and same_out and graph_same and ref_sel_ok and ref_err <= 2e-3) else 0],
+                        device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     return {"ok": bool(flag.item()), "ranks_same_selection": same_sel, "ranks_same_output": same_out,
+            "graph_replay_equal_to_eager": graph_same,
             "selection_equal_to_single_gpu": ref_sel_ok, "output_rel_err_vs_single_gpu": round(ref_err, 6),
             "layer": 0}
 

@@ -419,9 +419,11 @@ int32_t launch_decode(sd_index* x, int mode, int T, const void* q, const void* k
   p.gslot = x->gslot;
   p.gep = x->gep;
   const bool other_before = note_stream(st, x);
-  // Peer mode never overlaps launches: the exchange areas are reused by the
-  // next launch only after this one has finished everywhere.
-  const bool overlap = x->overlap && mode != sd::MODE_PEER;
+  // Peer mode overlaps too: the kernel reads the launch epoch and touches
+  // the exchange areas only after its grid-dependency wait, and a shard's
+  // launch finishes only once every CTA of every other shard has read this
+  // launch's lists (the shards' records it waits for come after them).
+  const bool overlap = x->overlap != 0;
   p.pdl_early = (overlap && other_before) ? 1 : 0;
   if (mode == sd::MODE_PEER) {
     for (int r = 0; r < comm->P; ++r) p.peer[r] = comm->peers[r];

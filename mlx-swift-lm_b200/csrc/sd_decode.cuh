@@ -901,10 +901,7 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
   const int Q = C * R, qrank = rep * C + crank;
   const int bh = blockIdx.y, b = bh / p.Hkv, h = bh % p.Hkv;
   const int K = p.K, P = p.P, pr = p.pr, S = p.S, T = p.T, NB = p.NB;
-  // Peer mode: this launch's epoch. The control word changes only after every
-  // CTA of the previous launch has finished, so all CTAs read the same value.
   const bool peer = p.mode == MODE_PEER;
-  const uint32_t epoch = peer ? *reinterpret_cast<const volatile uint32_t*>(p.peer[pr] + p.x_ctl) + 1u : 0u;
 
   float* qf = reinterpret_cast<float*>(sm + L.qf);
   float* qsum = reinterpret_cast<float*>(sm + L.qsum);
@@ -1037,6 +1034,11 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       for (int e = 0; e < EPL; ++e) rin[e] = p.racc_in[size_t(bh) * D + lane * EPL + e];
     }
   }
+  // Peer mode: this launch's epoch, read after the grid-dependency wait (the
+  // previous launch is complete). The control word changes only after every
+  // CTA of the previous launch has finished, so all CTAs read the same value;
+  // nothing touches an exchange area before this point.
+  const uint32_t epoch = peer ? *reinterpret_cast<const volatile uint32_t*>(p.peer[pr] + p.x_ctl) + 1u : 0u;
   // this launch's epoch of the group merge (the previous launch is complete)
   const uint32_t gep = Q > 1 ? __ldcg(p.gep + bh) + 1u : 0u;
   const E* qg = static_cast<const E*>(p.q) + (size_t(b) * p.Hq + size_t(h) * G) * D;
@@ -1586,8 +1588,11 @@ decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CU
       *issued = i + 1;
     };
     if (lane == 0) {
+      // the ring was last written by generic stores (the selection); the
+      // appended token's rows were fenced for the async proxy by the lanes
+      // that stored them, before the barriers since (no global fence here:
+      // in peer mode it would wait for this thread's stores to other GPUs)
       fence_proxy_async_shared();
-      fence_proxy_async_global();
       SD_STAMP_HERE(p, 21);
       for (int i = 0; i < min(nmine, F::kStages); ++i) {
         issue(i);
