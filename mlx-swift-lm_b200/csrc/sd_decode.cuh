@@ -3,8 +3,9 @@
 // Q CTAs serve one (batch, kv-head) group: C CTAs of a thread-block cluster
 // times R replica clusters (Q = C * R, all resident at once).
 //   phase 0  queries of the group -> shared memory; the group's summary rows
-//            are bulk-prefetched to L2 and the first register batch of them is
-//            loaded before the query barrier; the producer warp loads the new
+//            are bulk-prefetched to L2 (evict_first) and the first cp.async
+//            batches of them are staged before the query barrier; the producer
+//            warp loads the new
 //            token (the cache.update half of attentionWithCacheUpdate,
 //            Libraries/MLXLMCommon/AttentionUtils.swift:54-66 / :67-76).
 //   phase 1  score: 8 warps score this CTA's candidate rows, score[j] =
@@ -21,7 +22,8 @@
 //                      (DSMEM); every CTA runs the same block-wide bitonic
 //                      top-K (replica clusters repeat this);
 //            sliced -- otherwise: CTA q of Q scores chunk q, keeps its best MT
-//                      keys (bucket-histogram threshold), the lists meet in L2
+//                      keys (bitonic top-K for MT <= 128 of at most 2048,
+//                      else a bucket-histogram threshold), the lists meet in L2
 //                      as epoch-tagged message words, every CTA finds the
 //                      union's K-th key the same way and takes the union's keys
 //                      above it in gathered order; a CTA whose MT keys were all
@@ -34,13 +36,15 @@
 //            mbarrier-guarded stages; 8 consumer warps run online softmax in
 //            the exp2 domain on tensor cores (mma.sync m16n8k16) for 16-bit
 //            K/V and for 4/8-bit codes with 16-bit scales (exact codes as fp16
-//            operands), on FMA pipes otherwise.
+//            operands; 8-bit codes with the tokens as the tile's rows), on FMA
+//            pipes otherwise.
 //   phase 4  merge: warp partials -> CTA partial -> a few owner CTAs each
 //            gather every CTA's record of their output slice (L2 message words
 //            tagged with the group's epoch) and merge them by log-sum-exp; the
 //            other CTAs exit once their records are out.
-// Sharded decode: MODE_PEER exchanges the shards' candidates and partial
-// records through peer memory in the same launch; MODE_CANDIDATES /
+// Sharded decode: MODE_PEER exchanges the CTAs' lists (sliced groups; the
+// shards' top-K candidates otherwise) and the partial records through peer
+// memory in the same launch; MODE_CANDIDATES /
 // MODE_ATTEND run phases 0-2 and 2-4 around the caller's all-gathers.
 // Stage-4 semantics follow quantizedScaledDotProductAttention
 // (Libraries/MLXLMCommon/KVCache.swift:1544-1618) restricted to the gathered
